@@ -1,0 +1,399 @@
+#!/usr/bin/env python
+"""Benchmark of the sm_100a attention hot path; prints one JSON line (rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline workload (one step = one paged decode over all sessions of a rank):
+256 sessions per GPU, 32 query / 8 KV heads, head_dim 128, bf16 K/V in 16-token
+pages, context lengths U[1024, 32768], a 2048-token prefix shared by every
+session, page ids a random permutation of a pool sized 1.1x the demand.  The
+metric is decode attention HBM GB/s: algorithmic bytes (every K/V page touched,
+the shared prefix once, plus q, o, block-table entries and lengths) divided by
+the step time.  The pool (about 17 GB per GPU) is larger than L2, so nothing is
+flushed between steps.  Sessions are sharded: each rank runs its own 256
+sessions with no collective in the timed region (weak scaling); the step time is
+the max over ranks.
+
+The same line carries the causal GQA prefill op (B=8, Hq=32, Hkv=8, S=4096,
+D=128) as ``prefill`` with its TFLOP/s and tensor-core roofline, the end-to-end
+number through the public API with host buffers (``e2e``), the live roofline of
+the dominant kernel, the CPU baseline and the SM clocks sampled while timing.
+
+``--impl reference`` times the reference's CPU torch path for the same
+workload on the host cores (the EAGER ``scaled_dot_product_attention`` in fp32
+over pages gathered through the block table), on a bounded sample of sessions
+per step; under torchrun only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode-attn HBM GB/s"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+DECODE_WORKLOAD = ("paged decode: 256 sessions/GPU, 1 query token each, Hq=32 Hkv=8 D=128 bf16, "
+                   "16-token pages, L~U[1024,32768], 2048-token shared prefix, pool 1.1x demand, "
+                   "random page permutation")
+PREFILL_WORKLOAD = "causal GQA prefill: B=8 Hq=32 Hkv=8 S=4096 D=128 bf16, scale 1/sqrt(128)"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--pages-per-split", type=int, default=0)
+    ap.add_argument("--sessions", type=int, default=256)
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample", type=int, default=12, help="sessions in the CPU sample")
+    return ap.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    except Exception:
+        return dict(FALLBACK_PEAKS, source="fallback")
+
+
+def profile_traffic(name: str):
+    """Per-launch DRAM bytes of a kernel from its committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", name)
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples every 200 ms while timing."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_uuid: str):
+        self.uuid = gpu_uuid
+        self.proc = None
+        self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.uuid}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.out, stderr=subprocess.DEVNULL)
+        except (OSError, ValueError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        self.out.flush()
+
+    def summary(self):
+        try:
+            rows = [r.split(",") for r in open(self.out.name).read().strip().splitlines() if r]
+        finally:
+            os.unlink(self.out.name)
+        rows = [[c.strip() for c in r] for r in rows if len(r) >= 9]
+        if not rows:
+            return None
+        mhz = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())
+                if any(r[3].replace(".", "").isdigit() for r in rows) else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------- CPU legs
+def cpu_decode_sample(n_sample: int, seed: int, steps: int = 1):
+    """Time the reference's CPU decode path on n_sample sessions of the workload.
+
+    Sessions 0..n_sample-1 of the same length distribution, their prefix and own
+    pages generated on the CPU (values do not affect the timing).  Returns
+    (GB/s of algorithmic bytes, seconds per step, sample description, threads).
+    """
+    import torch
+    from oracle import attention as ora
+    from loopfuse_b200.workloads import PAGE, decode_lengths
+
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    lengths = decode_lengths(256, 1024, 32768, seed)[:n_sample]
+    n_pre = 2048 // PAGE
+    own = [max(0, math.ceil(L / PAGE) - n_pre) for L in lengths]
+    P = n_pre + sum(own)
+    g = torch.Generator().manual_seed(seed + 11)
+    kp = torch.randn((P, 8, PAGE, 128), generator=g).bfloat16()
+    vp = torch.randn((P, 8, PAGE, 128), generator=g).bfloat16()
+    q = torch.randn((n_sample, 32, 128), generator=g).bfloat16()
+    max_pages = max(math.ceil(L / PAGE) for L in lengths)
+    table = torch.full((n_sample, max_pages), -1, dtype=torch.int32)
+    cur = n_pre
+    for i, L in enumerate(lengths):
+        npg = math.ceil(L / PAGE)
+        row = list(range(min(npg, n_pre))) + list(range(cur, cur + own[i]))
+        cur += own[i]
+        table[i, :len(row)] = torch.tensor(row, dtype=torch.int32)
+    page_bytes = 2 * 8 * PAGE * 128 * 2
+    pre_used = max(min(math.ceil(L / PAGE), n_pre) for L in lengths)
+    nbytes = (pre_used + sum(own)) * page_bytes + 2 * n_sample * 32 * 128 * 2 + 4 * n_sample + \
+        4 * sum(math.ceil(L / PAGE) for L in lengths)
+    ora.decode_paged_sdpa(q[:1], kp, vp, table[:1], lengths[:1])      # warm the thread pool
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        ora.decode_paged_sdpa(q, kp, vp, table, lengths)
+        times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    desc = (f"{n_sample} of 256 sessions (lengths {min(lengths)}..{max(lengths)}), fp32 SDPA over "
+            f"pages gathered through the block table, {threads} threads, median of {steps}")
+    return nbytes / sec / 1e9, sec, desc, threads
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    n = max(1, min(args.cpu_sample, 8))
+    for _ in range(args.warmup):
+        cpu_decode_sample(n, args.seed, steps=1)
+    gbs, sec, desc, threads = cpu_decode_sample(n, args.seed, steps=max(1, args.steps))
+    line = {"metric": METRIC, "value": round(gbs, 4), "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": DECODE_WORKLOAD, "sample": desc},
+            "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads,
+                             "kind": "port", "sample": desc},
+            "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- GPU legs
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import torch
+    import torch.distributed as dist
+    from loopfuse_b200 import _lib
+    from loopfuse_b200 import attention as att
+    from loopfuse_b200.workloads import decode_bytes, decode_inputs, prefill_flops, prefill_inputs
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    peaks = load_peaks()
+    K, W = args.steps, max(3, args.warmup)
+
+    # ---------------- decode workload (headline) ----------------
+    w = decode_inputs(N=args.sessions, seed=args.seed + 1000 * rank, device=dev)
+    nb = decode_bytes(w)
+    N, Hq, D = w.q.shape
+    Hkv = w.k_pages.shape[1]
+    max_pages = w.block_table.shape[1]
+    pps = args.pages_per_split or att.default_pages_per_split(N, Hkv, max_pages)
+    ws = torch.empty(att.decode_workspace_bytes(N, Hq, D, max_pages, pps, w.n_prefix_pages),
+                     dtype=torch.uint8, device=dev)
+    out = torch.empty_like(w.q)
+
+    def step():
+        att.paged_decode(w.q, w.k_pages, w.v_pages, w.block_table, w.seq_lens,
+                         num_prefix_pages=w.n_prefix_pages, pages_per_split=pps, out=out,
+                         workspace=ws)
+
+    for _ in range(W):
+        step()
+    torch.cuda.synchronize()
+
+    uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+    stream = torch.cuda.current_stream()
+    split_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                for _ in range(K)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    lib = _lib.lib()
+    with ClockSampler(uuid) as clk:
+        barrier()
+        torch.cuda.synchronize()
+        t0.record(stream)
+        for i in range(K):
+            lib.lf_decode_set_profile_events(split_ev[i][0].cuda_event, split_ev[i][1].cuda_event)
+            step()
+        lib.lf_decode_set_profile_events(None, None)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    ms_local = t0.elapsed_time(t1) / K
+    split_ms = sum(a.elapsed_time(b) for a, b in split_ev) / K
+    ms = max_over_ranks(ms_local)
+    launches_per_step = 3 if w.n_prefix_pages else 2
+    n_prefix = w.n_prefix_pages
+    pool_gb = round(2 * w.k_pages.numel() * w.k_pages.element_size() / 1e9, 2)
+    value = world * nb["unique"] / (ms * 1e-3) / 1e9
+
+    # ---------------- end to end through the public API, host buffers ----------------
+    q_h = w.q.cpu().pin_memory()
+    bt_h = w.block_table.cpu().pin_memory()
+    ln_h = w.seq_lens.cpu().pin_memory()
+    o_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    q_d, bt_d, ln_d = torch.empty_like(w.q), torch.empty_like(w.block_table), torch.empty_like(w.seq_lens)
+
+    def e2e_step():
+        q_d.copy_(q_h, non_blocking=True)
+        bt_d.copy_(bt_h, non_blocking=True)
+        ln_d.copy_(ln_h, non_blocking=True)
+        att.paged_decode(q_d, w.k_pages, w.v_pages, bt_d, ln_d, num_prefix_pages=w.n_prefix_pages,
+                         pages_per_split=pps, out=out, workspace=ws)
+        o_h.copy_(out, non_blocking=True)
+
+    for _ in range(W):
+        e2e_step()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / K)
+    h2d = q_h.numel() * 2 + bt_h.numel() * 4 + ln_h.numel() * 4
+    d2h = o_h.numel() * 2
+
+    # ---------------- prefill op ----------------
+    prefill = None
+    if not args.no_prefill:
+        del w, ws, out, q_h, bt_h, ln_h, o_h, q_d, bt_d, ln_d
+        torch.cuda.empty_cache()
+        B, PHq, PHkv, S = 8, 32, 8, 4096
+        pq, pk, pv = prefill_inputs(B, PHq, PHkv, S, 128, seed=args.seed + 7 + 1000 * rank, device=dev)
+        flops = prefill_flops(B, PHq, S, 128)
+        for _ in range(W):
+            att.prefill_attention_fwd(pq, pk, pv, causal=True)
+        torch.cuda.synchronize()
+        pev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(K)]
+        barrier()
+        torch.cuda.synchronize()
+        for i in range(K):
+            pev[i][0].record(stream)
+            att.prefill_attention_fwd(pq, pk, pv, causal=True)
+            pev[i][1].record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        p_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in pev) / K)
+        tflops = flops / (p_ms * 1e-3) / 1e12
+        prefill = {"metric": "prefill TFLOP/s", "workload": PREFILL_WORKLOAD,
+                   "value": round(world * tflops, 2), "unit": "TFLOP/s", "ms_per_step": round(p_ms, 4),
+                   "flops_per_step": flops, "gpu_launches": K,
+                   "roofline": {"bound": "tensor", "achieved": round(tflops, 2),
+                                "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                                "frac": round(tflops / peaks["bf16_tflops"], 4),
+                                "traffic": profile_traffic("prefill_causal_b8_s4096.txt"),
+                                "peak_source": peaks["source"] + " (burst)"}}
+
+    # ---------------- CPU baseline (rank 0, N=1) ----------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        gbs, sec, desc, threads = cpu_decode_sample(args.cpu_sample, args.seed, steps=1)
+        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": desc}
+
+    if rank == 0:
+        split_bytes = nb["suffix_kv"]
+        achieved = split_bytes / (split_ms * 1e-3) / 1e9 if split_ms > 0 else None
+        clocks = clk.summary()
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded N(0,1) bf16 q and K/V pages, random page permutation",
+            "pct_of_8tbs": round(100 * value / world / 8000.0, 2),
+            "config": {"workload": DECODE_WORKLOAD, "sessions_per_gpu": N, "q_heads": Hq,
+                       "kv_heads": Hkv, "head_dim": D, "pages_per_split": pps,
+                       "prefix_pages": n_prefix, "pool_gb_per_gpu": pool_gb,
+                       "unique_bytes_per_step": nb["unique"], "logical_bytes_per_step": nb["logical"],
+                       "l2": "inputs larger than L2 (K/V pool ~17 GB per GPU); no flush",
+                       "parallelism": f"session-sharded x{world}, no collective in the timed region"},
+            "roofline": {"bound": "hbm", "kernel": "decode split (per-session pages)",
+                         "achieved": round(achieved, 1) if achieved else None,
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / peaks["hbm_gbs"], 4) if achieved else None,
+                         "traffic": profile_traffic("decode_split_256sess.txt"),
+                         "kernel_ms": round(split_ms, 4), "kernel_bytes": split_bytes,
+                         "op_frac": round(value / world / peaks["hbm_gbs"], 4),
+                         "peak_source": peaks["source"]},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(world * nb["unique"] / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                    "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches_per_step * K,
+            "clocks": clocks,
+            "prefill": prefill,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

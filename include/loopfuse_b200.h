@@ -1,0 +1,185 @@
+/*
+ * loopfuse_b200.h -- C ABI of the sm_100a attention hot path.
+ *
+ * One shared library, liblf_sm100.so, exports these symbols.  Signatures use
+ * plain pointers and sizes only: every device buffer is allocated by the caller
+ * (PyTorch's caching allocator in the Python host layer) and passed as a raw
+ * device pointer; `stream` is a cudaStream_t passed as void*.  Every call is
+ * asynchronous on that stream and returns a status code (LF_OK == 0) after
+ * validating its arguments on the host; lf_last_error() gives the message.
+ *
+ * Element types: K/V/Q/O are bf16 bit patterns (uint16_t).  Pool data copies
+ * (write / fork) move raw 2-byte elements and also serve fp16 pools.
+ *
+ * Reference interfaces replaced (paths inside the loopfuse repository):
+ *   prefill   kernels/triton/prefill_attn.py:127-168  prefill_attention_fwd
+ *             kernels/cuda/async_prefill.cu:56-236     agent_prefill_kernel,
+ *                                                      loopfuse_agent_prefill
+ *   decode    kernels/triton/decode_attn.py:133-171    decode_attention_fwd
+ *             kernels/cuda/ring_kv_cache.cu:120-248    ring_kv_decode_kernel
+ *   pool      runtime/kv_pool.py:103-198               KVPool.allocate_slot/
+ *                                                      write/release/read
+ *             kernels/cuda/ring_kv_cache.cu:69-109,282-297 ring_kv_write
+ *             kernels/cuda/_cuda_ext.py:60-116          ring_kv_write /
+ *                                                      async_zero_slot bindings
+ */
+#ifndef LOOPFUSE_B200_H
+#define LOOPFUSE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define LF_OK        0
+#define LF_EINVAL    1   /* bad shape, pointer, alignment or argument        */
+#define LF_ENOPAGES  2   /* pool has fewer free pages than requested         */
+#define LF_EOVERFLOW 3   /* a session would exceed max_pages_per_seq         */
+#define LF_ETIMEOUT  4   /* a bounded device-side wait gave up               */
+#define LF_ECUDA     5   /* a CUDA runtime call failed                       */
+
+#define LF_PAGE_SIZE 16  /* tokens per KV page */
+
+typedef uint16_t lf_bf16;
+
+/* Library version string and the message of the last failing call on this
+ * host thread (empty when the last call succeeded). */
+const char* lf_version(void);
+const char* lf_last_error(void);
+
+/* Reads and clears the library's device-side error word (synchronous).  A
+ * kernel whose bounded wait gave up (a pipeline barrier that never completed)
+ * records a non-zero site code there instead of hanging; *out == 0 means no
+ * kernel has reported a failure since the last call.  No reference
+ * counterpart: the reference kernels have no device-side error reporting. */
+int lf_device_status(int* out);
+
+/* ---- prefill attention --------------------------------------------------
+ * Replaces prefill_attention_fwd (kernels/triton/prefill_attn.py:127-168) and
+ * the host launcher loopfuse_agent_prefill (kernels/cuda/async_prefill.cu:220-236).
+ *
+ * o = softmax(scale * q k^T + mask) v for q [B,Hq,Sq,D], k/v [B,Hkv,Sk,D],
+ * o [B,Hq,Sq,D]; query head h reads KV head h / (Hq/Hkv).  causal != 0 masks
+ * key j for query i when j > i + (Sk - Sq) (the reference's q >= k mask when
+ * Sq == Sk, prefill_attn.py:97-99).  lse [B,Hq,Sq] (nullable) receives the
+ * natural-log log-sum-exp of each row.  D must be 128; all pointers 16-byte
+ * aligned.  tcgen05 MMA with TMEM accumulators, TMA-loaded tiles. */
+int lf_prefill_fwd(const lf_bf16* q, const lf_bf16* k, const lf_bf16* v, lf_bf16* o,
+                   float* lse, int batch, int num_q_heads, int num_kv_heads, int seq_q,
+                   int seq_k, int head_dim, float scale, int causal, void* stream);
+
+/* ---- paged split-KV decode ----------------------------------------------
+ * Replaces decode_attention_fwd (kernels/triton/decode_attn.py:133-171) and
+ * ring_kv_decode_kernel (kernels/cuda/ring_kv_cache.cu:120-248).
+ *
+ * One query token per session: q [N,Hq,D]; K/V pages [P,Hkv,16,D];
+ * block_table [N,max_pages] int32 page ids in token order; seq_lens [N] >= 1;
+ * o [N,Hq,D]; lse [N,Hq] (nullable, natural log).  Each session's pages are
+ * split into chunks of pages_per_split pages, processed by independent CTAs
+ * (GQA group of Hq/Hkv heads per CTA, 128-bit coalesced page reads, warp
+ * shuffle reductions) and merged by log-sum-exp.  num_prefix_pages > 0 says
+ * the first num_prefix_pages block-table entries are the same pages for every
+ * session (a forked shared prefix): they are read once per group of sessions
+ * instead of once per session.  workspace holds the split partials; its size
+ * comes from lf_decode_workspace_size.  D must be 128 (or 64).  A length
+ * past max_pages*16 is clamped and a page id outside [0, num_pages) is
+ * replaced by page 0; either is reported through lf_device_status(). */
+int lf_decode_workspace_size(int num_seqs, int num_q_heads, int head_dim, int max_pages,
+                             int pages_per_split, int num_prefix_pages, size_t* bytes);
+int lf_decode_fwd(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* v_pages,
+                  const int32_t* block_table, const int32_t* seq_lens, int num_prefix_pages,
+                  lf_bf16* o, float* lse, void* workspace, size_t workspace_bytes,
+                  int num_seqs, int num_q_heads, int num_kv_heads, int head_dim,
+                  int num_pages, int max_pages, int pages_per_split, float scale,
+                  void* stream);
+
+/* Instrumentation for timing the dominant decode kernel: while both events
+ * are non-null, every lf_decode_fwd records ev_begin right before and ev_end
+ * right after its per-session split kernel, on the call's stream (events are
+ * cudaEvent_t passed as void*).  Pass two nulls to stop.  No work is skipped
+ * or changed.  No reference counterpart (the reference has no decode launch
+ * to time). */
+int lf_decode_set_profile_events(void* ev_begin, void* ev_end);
+
+/* ---- paged KV pool --------------------------------------------------------
+ * Device-resident metadata of a paged, refcounted KV pool.  Replaces the
+ * dense slot pool of runtime/kv_pool.py:28-235 (allocate_slot :103, release
+ * :117, write :123, read :151) and the ring-buffer write of
+ * kernels/cuda/ring_kv_cache.cu:69-109.  All arrays are device memory owned
+ * by the caller.  Semantics (FIFO free queue, all-or-nothing allocation,
+ * refcounted sharing, free order) are specified by the pool oracle and
+ * reproduced bit for bit.
+ *
+ * Errors found on the device (ENOPAGES, EOVERFLOW) are written to
+ * ctrl[LF_CTRL_STATUS]; the status is sticky: every later pool call is a no-op
+ * until lf_pool_clear_status.  Reading it is the caller's one host sync. */
+#define LF_CTRL_HEAD   0   /* queue index of the first free page           */
+#define LF_CTRL_COUNT  1   /* number of free pages                         */
+#define LF_CTRL_STATUS 2   /* sticky device status (LF_OK when fine)       */
+#define LF_CTRL_WORDS  8
+
+typedef struct lf_pool_meta {
+    int32_t* free_queue;    /* [num_pages] ring of free page ids             */
+    int32_t* refcount;      /* [num_pages]                                   */
+    int32_t* block_table;   /* [max_seqs * max_pages_per_seq], -1 = no page  */
+    int32_t* seq_len;       /* [max_seqs] tokens held per session            */
+    int32_t* ctrl;          /* [LF_CTRL_WORDS]                               */
+    int32_t* scratch;       /* [num_pages] kept at INT32_MAX between calls   */
+    int32_t num_pages;
+    int32_t max_seqs;
+    int32_t max_pages_per_seq;
+    int32_t page_size;      /* must be LF_PAGE_SIZE                          */
+} lf_pool_meta;
+
+/* Reset to: queue 0..P-1, refcounts 0, tables -1, lengths 0, status OK. */
+int lf_pool_init(const lf_pool_meta* m, void* stream);
+int lf_pool_clear_status(const lf_pool_meta* m, void* stream);
+
+/* Allocation step of append: session seq_ids[i] grows by n_new[i] tokens,
+ * taking ceil-page deltas from the queue head in order; start_pos[i] receives
+ * its old length.  All or nothing.  seq_ids must be distinct. */
+int lf_pool_reserve(const lf_pool_meta* m, const int32_t* seq_ids, const int32_t* n_new, int n,
+                    int32_t* start_pos, void* stream);
+
+/* Data step of append: token t of session i (rows cu_tokens[i] ..
+ * cu_tokens[i+1]-1 of k_new/v_new) goes to position start_pos[i] + t.
+ * k_new element (layer l, token t, head h, dim d) is at
+ * l*stride_layer + t*stride_token + h*stride_head + d (elements).  Pages are
+ * [num_layers][num_pages][Hkv][16][D]. */
+int lf_pool_write_kv(const lf_pool_meta* m, const int32_t* seq_ids, const int32_t* start_pos,
+                     const int32_t* cu_tokens, int n, int total_tokens, const void* k_new,
+                     const void* v_new,
+                     int64_t stride_layer, int64_t stride_token, int64_t stride_head,
+                     void* k_pages, void* v_pages, int num_layers, int num_kv_heads,
+                     int head_dim, void* stream);
+
+/* Share src's first prefix_len tokens with each (empty) dst: full pages by
+ * reference (refcount += 1 each), a partial last page copied into a fresh
+ * page per destination. */
+int lf_pool_fork(const lf_pool_meta* m, int src_seq, const int32_t* dst_seqs, int n,
+                 int prefix_len, void* k_pages, void* v_pages, int num_layers,
+                 int num_kv_heads, int head_dim, void* stream);
+
+/* Release sessions: refcount -1 per page occurrence; pages reaching zero go to
+ * the queue tail in first-occurrence order; rows reset. */
+int lf_pool_free(const lf_pool_meta* m, const int32_t* seq_ids, int n, void* stream);
+
+/* Batch block table: out_table[i*out_stride + j] = table row of seq_ids[i]
+ * (j < out_stride), out_lens[i] = its length. */
+int lf_pool_gather(const lf_pool_meta* m, const int32_t* seq_ids, int n, int32_t* out_table,
+                   int out_stride, int32_t* out_lens, void* stream);
+
+/* Copy one session's tokens [start, end) of one layer out of the pages into
+ * dense k_out/v_out [Hkv][end-start][D] (the reference's read(), :151-165). */
+int lf_pool_read(const lf_pool_meta* m, int seq, int layer, int start, int end,
+                 const void* k_pages, const void* v_pages, void* k_out, void* v_out,
+                 int num_layers, int num_kv_heads, int head_dim, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LOOPFUSE_B200_H */

@@ -1,0 +1,357 @@
+// Paged split-KV decode attention for sm_100a.
+//
+// Replaces the reference's decode_attention_fwd (kernels/triton/decode_attn.py:133-171,
+// one program per (batch, head) over a contiguous cache) and the non-compiling
+// ring_kv_decode_kernel (kernels/cuda/ring_kv_cache.cu:120-248).
+//
+// Work split.  CTA (split, kv_head, session) owns pages_per_split consecutive pages of one
+// session's block-table row and the Hq/Hkv query heads that share kv_head (GQA): every K/V
+// byte is read once for the whole group.  Four warps take the CTA's pages round-robin.
+// A page of one head is 16 rows x D bf16 = 4 KB contiguous; a warp reads it with 16-byte
+// loads, D/8 lanes per row, so each load instruction covers whole, adjacent rows.
+//
+// Per page a lane holds 8 dims of TPI tokens per instruction row.  q.k partial sums are
+// reduced over the D/8 lanes of a row with a reduce-scatter (each halving step exchanges
+// half of the group's heads), so a lane ends with the full score of one (token, head).
+// Online softmax runs in the log2 domain (q pre-scaled by scale*log2 e).  The warp's
+// running (max, sum, acc) are merged across warps through shared memory, and the CTA
+// writes one unnormalised partial (o, max, sum) per query head.  The combine kernel
+// merges a session's partials by log-sum-exp.
+#include "decode_common.cuh"
+
+#include <math.h>
+
+namespace lf {
+namespace decode {
+
+// part_o: [N, Hq, n_slots, D] fp32 (unnormalised); part_ml: [N, Hq, n_slots] (max, sum),
+// max in log2 units of the scaled scores.
+template <int D, int G>
+__global__ void __launch_bounds__(kThreads)
+split_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kp,
+             const uint16_t* __restrict__ vp, const int32_t* __restrict__ bt,
+             const int32_t* __restrict__ seq_lens, float* __restrict__ part_o,
+             float2* __restrict__ part_ml, int Hq, int Hkv, int num_pages, int max_pages,
+             int pages_per_split, int first_page, int n_slots, float qscale) {
+    using C = Cfg<D, G>;
+    const int split = blockIdx.x, h = blockIdx.y, n = blockIdx.z;
+    const int L = min(max(seq_lens[n], 0), max_pages * kPage);
+    const int npages = (L + kPage - 1) / kPage;
+    const int p_begin = first_page + split * pages_per_split;
+    if (p_begin >= npages) return;
+    const int p_end = min(p_begin + pages_per_split, npages);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c = lane % C::LPT;
+    const int sub = lane / C::LPT;
+    const int hl = head_of_chunk<D, G>(c);
+
+    float qf[G][8];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(q + ((size_t)n * Hq + h * G + g) * D + 8 * c);
+        unpack8(raw, qf[g]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) qf[g][j] *= qscale;
+    }
+    float acc[G][8];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[g][j] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
+
+    const int32_t* bt_row = bt + (size_t)n * max_pages;
+    for (int pi = p_begin + warp; pi < p_end; pi += kWarps) {
+        const int page = checked_page(bt_row[pi], num_pages);
+        const size_t base = ((size_t)page * Hkv + h) * (size_t)(kPage * D);
+        const uint16_t* kb = kp + base + sub * D + 8 * c;
+        const uint16_t* vb = vp + base + sub * D + 8 * c;
+        uint4 kr[C::ROWS], vr[C::ROWS];
+#pragma unroll
+        for (int r = 0; r < C::ROWS; ++r) kr[r] = ldg_stream(kb + r * C::TPI * D);
+#pragma unroll
+        for (int r = 0; r < C::ROWS; ++r) vr[r] = ldg_stream(vb + r * C::TPI * D);
+
+        const int tok0 = pi * kPage + sub;
+        float s[C::ROWS];
+#pragma unroll
+        for (int r = 0; r < C::ROWS; ++r) {
+            float kf[8];
+            unpack8(kr[r], kf);
+            float part[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                float a = 0.f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) a = fmaf(qf[g][j], kf[j], a);
+                part[g] = a;
+            }
+            const float sc = reduce_scatter_row<D, G>(part, c);
+            s[r] = (tok0 + r * C::TPI < L) ? sc : -INFINITY;
+        }
+        float mx = s[0];
+#pragma unroll
+        for (int r = 1; r < C::ROWS; ++r) mx = fmaxf(mx, s[r]);
+#pragma unroll
+        for (int off = C::LPT; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        // Every page below npages holds at least one valid token, so m_new is finite.
+        const float m_new = fmaxf(m_run, mx);
+        const float alpha = fast_exp2(m_run - m_new);
+        float p[C::ROWS];
+        float ps = 0.f;
+#pragma unroll
+        for (int r = 0; r < C::ROWS; ++r) {
+            p[r] = fast_exp2(s[r] - m_new);
+            ps += p[r];
+        }
+#pragma unroll
+        for (int off = C::LPT; off < 32; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+        l_run = l_run * alpha + ps;
+        m_run = m_new;
+
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float ag = __shfl_sync(0xffffffffu, alpha, chunk_of_head<D, G>(g));
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[g][j] *= ag;
+        }
+#pragma unroll
+        for (int r = 0; r < C::ROWS; ++r) {
+            float vf[8];
+            unpack8(vr[r], vf);
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float pg = __shfl_sync(0xffffffffu, p[r], sub * C::LPT + chunk_of_head<D, G>(g));
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[g][j] = fmaf(pg, vf[j], acc[g][j]);
+            }
+        }
+    }
+
+    // Sum the token-row sub-groups of the warp.
+#pragma unroll
+    for (int off = C::LPT; off < 32; off <<= 1)
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[g][j] += __shfl_xor_sync(0xffffffffu, acc[g][j], off);
+
+    __shared__ float sm_m[kWarps][G], sm_l[kWarps][G];
+    __shared__ float sm_acc[kWarps][G][D];
+    if (sub == 0) {
+        if (c == chunk_of_head<D, G>(hl)) {
+            sm_m[warp][hl] = m_run;
+            sm_l[warp][hl] = l_run;
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) sm_acc[warp][g][8 * c + j] = acc[g][j];
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < G * D; idx += kThreads) {
+        const int g = idx / D, d = idx % D;
+        float M = sm_m[0][g];
+#pragma unroll
+        for (int w = 1; w < kWarps; ++w) M = fmaxf(M, sm_m[w][g]);
+        float o = 0.f, l = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) {
+            const float sc = fast_exp2(sm_m[w][g] - M);
+            o = fmaf(sc, sm_acc[w][g][d], o);
+            l = fmaf(sc, sm_l[w][g], l);
+        }
+        const size_t slot = ((size_t)n * Hq + h * G + g) * n_slots + split;
+        part_o[slot * D + d] = o;
+        if (d == 0) part_ml[slot] = make_float2(M, l);
+    }
+}
+
+// One CTA of D/4 threads per (query head, session): merge the session's used slots.
+template <int D>
+__global__ void __launch_bounds__(D / 4)
+combine_kernel(const float* __restrict__ part_o, const float2* __restrict__ part_ml,
+               const int32_t* __restrict__ seq_lens, uint16_t* __restrict__ o,
+               float* __restrict__ lse, int Hq, int max_pages, int pages_per_split,
+               int first_page, int n_slots, int prefix_slot0, int n_prefix_chunks) {
+    const int hq = blockIdx.x, n = blockIdx.y;
+    const int L = min(max(seq_lens[n], 0), max_pages * kPage);
+    const int npages = (L + kPage - 1) / kPage;
+    const int rem = npages - first_page;
+    const int nsplit = rem > 0 ? (rem + pages_per_split - 1) / pages_per_split : 0;
+    const size_t row = (size_t)n * Hq + hq;
+    const float2* ml = part_ml + row * n_slots;
+    const float* po = part_o + row * n_slots * D;
+
+    const int npre = L > 0 ? n_prefix_chunks : 0;
+    float M = -INFINITY;
+    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, ml[s].x);
+    for (int s = 0; s < npre; ++s) M = fmaxf(M, ml[prefix_slot0 + s].x);
+
+    const int d0 = threadIdx.x * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float l = 0.f;
+    auto add_slot = [&](int s) {
+        const float2 e = ml[s];
+        const float w = fast_exp2(e.x - M);
+        const float4 v = *reinterpret_cast<const float4*>(po + (size_t)s * D + d0);
+        acc.x = fmaf(w, v.x, acc.x); acc.y = fmaf(w, v.y, acc.y);
+        acc.z = fmaf(w, v.z, acc.z); acc.w = fmaf(w, v.w, acc.w);
+        l = fmaf(w, e.y, l);
+    };
+    for (int s = 0; s < nsplit; ++s) add_slot(s);
+    for (int s = 0; s < npre; ++s) add_slot(prefix_slot0 + s);
+
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    uint2 packed;
+    packed.x = pack_bf16x2(acc.x * inv, acc.y * inv);
+    packed.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+    *reinterpret_cast<uint2*>(o + row * D + d0) = packed;
+    if (lse != nullptr && threadIdx.x == 0) lse[row] = l > 0.f ? (M + log2f(l)) * kLn2 : -INFINITY;
+}
+
+template <int D, int G>
+void launch_split(dim3 grid, cudaStream_t st, const uint16_t* q, const uint16_t* kp,
+                  const uint16_t* vp, const int32_t* bt, const int32_t* lens, float* po,
+                  float2* pml, int Hq, int Hkv, int num_pages, int max_pages, int pps,
+                  int first_page, int n_slots, float qscale) {
+    split_kernel<D, G><<<grid, kThreads, 0, st>>>(q, kp, vp, bt, lens, po, pml, Hq, Hkv, num_pages,
+                                                  max_pages, pps, first_page, n_slots, qscale);
+}
+
+template <int D>
+int dispatch_group(int G, dim3 grid, cudaStream_t st, const uint16_t* q, const uint16_t* kp,
+                   const uint16_t* vp, const int32_t* bt, const int32_t* lens, float* po,
+                   float2* pml, int Hq, int Hkv, int num_pages, int max_pages, int pps,
+                   int first_page, int n_slots, float qscale) {
+    switch (G) {
+        case 1: launch_split<D, 1>(grid, st, q, kp, vp, bt, lens, po, pml, Hq, Hkv, num_pages, max_pages, pps, first_page, n_slots, qscale); break;
+        case 2: launch_split<D, 2>(grid, st, q, kp, vp, bt, lens, po, pml, Hq, Hkv, num_pages, max_pages, pps, first_page, n_slots, qscale); break;
+        case 4: launch_split<D, 4>(grid, st, q, kp, vp, bt, lens, po, pml, Hq, Hkv, num_pages, max_pages, pps, first_page, n_slots, qscale); break;
+        case 8: launch_split<D, 8>(grid, st, q, kp, vp, bt, lens, po, pml, Hq, Hkv, num_pages, max_pages, pps, first_page, n_slots, qscale); break;
+        default: return set_error(LF_EINVAL, "decode: Hq/Hkv must be 1, 2, 4 or 8 (got %d)", G);
+    }
+    return LF_OK;
+}
+
+// Slots [0, suffix_splits) hold the per-session splits after the prefix; slots
+// [suffix_splits, suffix_splits + prefix_chunks) hold the shared-prefix chunks.
+inline int suffix_splits(int max_pages, int pps, int n_prefix) {
+    return (max_pages - n_prefix + pps - 1) / pps;
+}
+inline int prefix_chunks(int pps, int n_prefix) { return (n_prefix + pps - 1) / pps; }
+inline int num_slots(int max_pages, int pages_per_split, int num_prefix_pages) {
+    return suffix_splits(max_pages, pages_per_split, num_prefix_pages) +
+           prefix_chunks(pages_per_split, num_prefix_pages);
+}
+
+}  // namespace decode
+}  // namespace lf
+
+using namespace lf;
+
+extern "C" int lf_decode_workspace_size(int num_seqs, int num_q_heads, int head_dim,
+                                        int max_pages, int pages_per_split, int num_prefix_pages,
+                                        size_t* bytes) {
+    LF_CHECK_ARG(bytes != nullptr, "decode: bytes is null");
+    LF_CHECK_ARG(num_seqs >= 0 && num_q_heads > 0 && head_dim > 0 && max_pages > 0 &&
+                     pages_per_split > 0 && num_prefix_pages >= 0,
+                 "decode: bad workspace arguments");
+    const size_t slots = (size_t)decode::num_slots(max_pages, pages_per_split, num_prefix_pages);
+    *bytes = (size_t)num_seqs * num_q_heads * slots * ((size_t)head_dim * sizeof(float) + sizeof(float2));
+    clear_error();
+    return LF_OK;
+}
+
+// Defined in decode_prefix.cu: shared-prefix partials, one pass over the prefix pages per
+// group of sessions.
+namespace lf { namespace decode {
+int launch_prefix(const uint16_t* q, const uint16_t* kp, const uint16_t* vp, const int32_t* bt,
+                  const int32_t* lens, float* po, float2* pml, int N, int Hq, int Hkv, int D,
+                  int num_pages, int max_pages, int n_prefix, int pages_per_chunk, int n_slots,
+                  int slot0, float qscale, cudaStream_t st);
+}}
+
+static cudaEvent_t g_prof_begin = nullptr, g_prof_end = nullptr;
+
+extern "C" int lf_decode_set_profile_events(void* ev_begin, void* ev_end) {
+    g_prof_begin = static_cast<cudaEvent_t>(ev_begin);
+    g_prof_end = static_cast<cudaEvent_t>(ev_end);
+    clear_error();
+    return LF_OK;
+}
+
+extern "C" int lf_decode_fwd(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* v_pages,
+                             const int32_t* block_table, const int32_t* seq_lens,
+                             int num_prefix_pages, lf_bf16* o, float* lse, void* workspace,
+                             size_t workspace_bytes, int num_seqs, int num_q_heads,
+                             int num_kv_heads, int head_dim, int num_pages, int max_pages,
+                             int pages_per_split, float scale, void* stream) {
+    LF_CHECK_ARG(q && k_pages && v_pages && block_table && seq_lens && o && workspace,
+                 "decode: null pointer argument");
+    LF_CHECK_ARG(aligned16(q) && aligned16(k_pages) && aligned16(v_pages) && aligned16(o) &&
+                     aligned16(workspace),
+                 "decode: q, pages, o and workspace must be 16-byte aligned");
+    LF_CHECK_ARG(head_dim == 128 || head_dim == 64, "decode: head_dim must be 64 or 128 (got %d)",
+                 head_dim);
+    LF_CHECK_ARG(num_seqs > 0 && num_kv_heads > 0 && num_q_heads % num_kv_heads == 0,
+                 "decode: need num_seqs > 0 and Hq a multiple of Hkv");
+    LF_CHECK_ARG(num_pages > 0 && max_pages > 0 && pages_per_split > 0,
+                 "decode: num_pages, max_pages and pages_per_split must be > 0");
+    LF_CHECK_ARG(num_prefix_pages >= 0 && num_prefix_pages <= max_pages,
+                 "decode: num_prefix_pages out of range");
+    LF_CHECK_ARG(num_seqs <= 65535 && num_kv_heads <= 65535, "decode: grid limits exceeded");
+    size_t need = 0;
+    lf_decode_workspace_size(num_seqs, num_q_heads, head_dim, max_pages, pages_per_split,
+                             num_prefix_pages, &need);
+    LF_CHECK_ARG(workspace_bytes >= need, "decode: workspace too small (%zu < %zu bytes)",
+                 workspace_bytes, need);
+
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int G = num_q_heads / num_kv_heads;
+    const int n_slots = decode::num_slots(max_pages, pages_per_split, num_prefix_pages);
+    const int max_split = decode::suffix_splits(max_pages, pages_per_split, num_prefix_pages);
+    const int n_prefix_chunks = decode::prefix_chunks(pages_per_split, num_prefix_pages);
+    float* po = static_cast<float*>(workspace);
+    float2* pml = reinterpret_cast<float2*>(po + (size_t)num_seqs * num_q_heads * n_slots * head_dim);
+    const float qscale = scale * kLog2e;
+    const uint16_t* q16 = q;
+
+    if (num_prefix_pages > 0) {
+        int rc = decode::launch_prefix(q16, k_pages, v_pages, block_table, seq_lens, po, pml,
+                                       num_seqs, num_q_heads, num_kv_heads, head_dim, num_pages,
+                                       max_pages, num_prefix_pages, pages_per_split, n_slots, max_split,
+                                       qscale, st);
+        if (rc != LF_OK) return rc;
+    }
+    const bool prof = g_prof_begin != nullptr && g_prof_end != nullptr;
+    if (prof) LF_CHECK_CUDA(cudaEventRecord(g_prof_begin, st));
+    if (max_split > 0) {
+        dim3 grid(max_split, num_kv_heads, num_seqs);
+        LF_CHECK_ARG(max_split <= 2147483647, "decode: too many splits");
+        int rc = head_dim == 128
+                     ? decode::dispatch_group<128>(G, grid, st, q16, k_pages, v_pages, block_table,
+                                                   seq_lens, po, pml, num_q_heads, num_kv_heads,
+                                                   num_pages, max_pages, pages_per_split, num_prefix_pages,
+                                                   n_slots, qscale)
+                     : decode::dispatch_group<64>(G, grid, st, q16, k_pages, v_pages, block_table,
+                                                  seq_lens, po, pml, num_q_heads, num_kv_heads,
+                                                  num_pages, max_pages, pages_per_split, num_prefix_pages,
+                                                  n_slots, qscale);
+        if (rc != LF_OK) return rc;
+        rc = launch_status("decode split");
+        if (rc != LF_OK) return rc;
+    }
+    if (prof) LF_CHECK_CUDA(cudaEventRecord(g_prof_end, st));
+    dim3 cgrid(num_q_heads, num_seqs);
+    if (head_dim == 128)
+        decode::combine_kernel<128><<<cgrid, 32, 0, st>>>(po, pml, seq_lens, o, lse, num_q_heads,
+                                                          max_pages, pages_per_split, num_prefix_pages,
+                                                          n_slots, max_split, n_prefix_chunks);
+    else
+        decode::combine_kernel<64><<<cgrid, 16, 0, st>>>(po, pml, seq_lens, o, lse, num_q_heads,
+                                                         max_pages, pages_per_split, num_prefix_pages,
+                                                         n_slots, max_split, n_prefix_chunks);
+    return launch_status("decode combine");
+}

@@ -1,0 +1,2 @@
+from .base import Pass, PassManager, PassResult
+from .phase_select import PHASE_KERNEL_MAP, PhaseSelectPass, resolve_kernel

@@ -1,0 +1,366 @@
+"""Paged, refcounted KV pool in device memory -- drop-in for ``runtime/kv_pool.py``.
+
+The reference pool (``runtime/kv_pool.py:28-235``) preallocates one dense
+``[max_seq_len]`` strip per slot.  This pool keeps the same public API and
+error behaviour but stores K/V in 16-token pages that sessions can share:
+
+* ``allocate_slot`` / ``release`` / ``write`` / ``read`` / ``read_all_layers``
+  / ``prefetch_next_slot`` / ``stats`` / ``hbm_usage_bytes`` / ``from_config``
+  behave as in the reference: slots are FIFO (``:103-121``), ``write`` appends
+  at ``current_len`` and returns the new length (``:123-149``), overflow and
+  exhaustion raise ``RuntimeError`` with the reference's messages
+  (``:105-109``, ``:135-139``), ``read`` returns ``[H, S, D]`` (a gathered
+  copy, since pages are not contiguous).
+* New paged API: ``alloc``, ``append`` (batched), ``fork`` (share a prefix by
+  reference), ``free``, ``block_table`` (batch table for ``paged_decode``),
+  ``layer_pages``, ``snapshot``.
+
+Every metadata operation (page allocation, fork, free, block-table gather) is
+a device kernel from ``liblf_sm100.so`` launched on the pool's stream; no
+CPU-side page bookkeeping exists.  K/V storage is ``[L, P, Hkv, 16, D]`` per
+tensor: one layer's pages are ``[P, Hkv, 16, D]``, a page of one head 4 KB
+contiguous at D = 128.
+
+The pool lives on the GPU only: ``device`` must be CUDA.
+"""
+from __future__ import annotations
+
+import math
+from typing import Dict, List, Optional, Sequence, Tuple, Union
+
+import torch
+
+from .. import _lib
+from .._lib import LF_PAGE_SIZE, LoopfuseError, PoolMeta
+
+_DTYPES = {"bf16": torch.bfloat16, "fp16": torch.float16}
+
+
+class KVState:
+    """Handle to one session (trajectory) in the pool: ``slot_id`` is its block-table row."""
+
+    def __init__(self, slot_id: int, pool: "KVPool"):
+        self.slot_id = slot_id
+        self.pool = pool
+        self.current_len = 0
+        self.step_id = 0
+
+    @property
+    def seq_id(self) -> int:
+        return self.slot_id
+
+    def advance_step(self) -> None:
+        self.step_id += 1
+
+    def __repr__(self):
+        return f"KVState(slot={self.slot_id}, len={self.current_len}, step={self.step_id})"
+
+
+class KVPool:
+    def __init__(self, num_layers: int, num_heads: int, head_dim: int, max_seq_len: int,
+                 max_slots: int = 8, dtype: torch.dtype = torch.float16, device: str = "cuda",
+                 num_kv_heads: Optional[int] = None, num_pages: Optional[int] = None):
+        dev = torch.device(device)
+        if dev.type != "cuda":
+            raise LoopfuseError(_lib.LF_EINVAL, "loopfuse_b200.KVPool keeps its pages and metadata "
+                                                "in GPU memory; device must be CUDA")
+        if dtype not in (torch.bfloat16, torch.float16):
+            raise LoopfuseError(_lib.LF_EINVAL, f"pool dtype must be bf16 or fp16, got {dtype}")
+        if dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        self.num_layers = num_layers
+        self.num_heads = num_heads
+        self.num_kv_heads = num_kv_heads or num_heads
+        self.head_dim = head_dim
+        self.max_seq_len = max_seq_len
+        self.max_slots = max_slots
+        self.dtype = dtype
+        self.device = dev
+        self.page_size = LF_PAGE_SIZE
+        self.max_pages_per_seq = math.ceil(max_seq_len / LF_PAGE_SIZE)
+        self.num_pages = num_pages or max_slots * self.max_pages_per_seq
+
+        shape = (num_layers, self.num_pages, self.num_kv_heads, LF_PAGE_SIZE, head_dim)
+        self.keys = torch.zeros(shape, dtype=dtype, device=dev)
+        self.values = torch.zeros(shape, dtype=dtype, device=dev)
+
+        i32 = dict(dtype=torch.int32, device=dev)
+        self._free_queue = torch.empty(self.num_pages, **i32)
+        self._refcount = torch.empty(self.num_pages, **i32)
+        self._table = torch.empty(max_slots * self.max_pages_per_seq, **i32)
+        self._seq_len = torch.empty(max_slots, **i32)
+        self._ctrl = torch.zeros(_lib.LF_CTRL_WORDS, **i32)
+        self._scratch = torch.empty(self.num_pages, **i32)
+        self._meta = PoolMeta(self._free_queue.data_ptr(), self._refcount.data_ptr(),
+                              self._table.data_ptr(), self._seq_len.data_ptr(),
+                              self._ctrl.data_ptr(), self._scratch.data_ptr(), self.num_pages,
+                              max_slots, self.max_pages_per_seq, LF_PAGE_SIZE)
+        # Same two-stream arrangement as the reference (kv_pool.py:76-81): compute stays hot,
+        # background work (speculative prefill) goes to the low-priority stream.
+        self.compute_stream = torch.cuda.Stream(device=dev, priority=0)
+        self.prefetch_stream = torch.cuda.Stream(device=dev, priority=-1)
+        self._oversubscribed = self.num_pages < max_slots * self.max_pages_per_seq
+
+        self._free_slots: List[int] = list(range(max_slots))
+        self._active: Dict[int, KVState] = {}
+        self._write_count = 0
+        self._bytes_written = 0
+        with torch.cuda.device(dev):
+            self._call("lf_pool_init", self._meta_ref(), self._stream())
+
+    # -- construction --------------------------------------------------------
+    @classmethod
+    def from_config(cls, kv_config: dict, device: str = "cuda", max_slots: int = 8,
+                    num_pages: Optional[int] = None) -> "KVPool":
+        return cls(num_layers=kv_config["num_layers"], num_heads=kv_config["num_heads"],
+                   head_dim=kv_config["head_dim"], max_seq_len=kv_config["max_seq_len"],
+                   dtype=_DTYPES.get(kv_config.get("dtype", "fp16"), torch.float16),
+                   device=device, max_slots=max_slots,
+                   num_kv_heads=kv_config.get("num_kv_heads"), num_pages=num_pages)
+
+    # -- plumbing -------------------------------------------------------------
+    def _meta_ref(self):
+        return _lib.ctypes.byref(self._meta)
+
+    def _stream(self, stream: Optional[torch.cuda.Stream] = None) -> int:
+        return (stream or torch.cuda.current_stream(self.device)).cuda_stream
+
+    def _call(self, name: str, *args) -> None:
+        _lib.call(name, *args)
+
+    def _ids(self, xs: Sequence[int]) -> torch.Tensor:
+        return torch.tensor(list(xs), dtype=torch.int32).to(self.device, non_blocking=True)
+
+    def status(self) -> int:
+        """Sticky device status (one host sync)."""
+        return int(self._ctrl[_lib.LF_CTRL_STATUS].item())
+
+    def _raise_if_failed(self, what: str, detail: str = "") -> None:
+        st = self.status()
+        if st == _lib.LF_OK:
+            return
+        self._call("lf_pool_clear_status", self._meta_ref(), self._stream())
+        if st == _lib.LF_ENOPAGES:
+            raise RuntimeError(f"KVPool exhausted: no free pages for {what} "
+                               f"({self.num_pages} pages). {detail}".strip())
+        if st == _lib.LF_EOVERFLOW:
+            raise RuntimeError(f"KV cache overflow in {what}. {detail}".strip())
+        raise LoopfuseError(st, f"pool {what} failed on the device. {detail}".strip())
+
+    # -- reference API ----------------------------------------------------------
+    def allocate_slot(self) -> KVState:
+        """Start a trajectory: FIFO slot (reference ``kv_pool.py:103-115``)."""
+        if not self._free_slots:
+            raise RuntimeError(f"KVPool exhausted: all {self.max_slots} slots in use. "
+                               f"Increase max_slots or wait for a trajectory to complete.")
+        slot = self._free_slots.pop(0)
+        state = KVState(slot, self)
+        self._active[slot] = state
+        return state
+
+    def release(self, state: KVState) -> None:
+        """End a trajectory: its pages are dereferenced on the device, the slot recycled."""
+        if state.slot_id in self._active:
+            self.free(state)
+            del self._active[state.slot_id]
+            self._free_slots.append(state.slot_id)
+
+    def write(self, state: KVState, new_keys: torch.Tensor, new_values: torch.Tensor,
+              stream: Optional[torch.cuda.Stream] = None) -> int:
+        """Append ``[L, Hkv, S_new, D]`` keys/values at ``current_len``; returns the new length."""
+        seq_new = new_keys.shape[2]
+        if state.current_len + seq_new > self.max_seq_len:
+            raise RuntimeError(f"KV cache overflow: current_len={state.current_len} + "
+                               f"seq_new={seq_new} > max_seq_len={self.max_seq_len}")
+        self.append([state], [new_keys], [new_values], layout="lhsd", stream=stream)
+        return state.current_len
+
+    def read(self, state: KVState, layer: int, seq_start: int = 0,
+             seq_end: Optional[int] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Gathered copy of one layer's keys/values, ``[Hkv, seq_range, D]``."""
+        seq_end = seq_end or state.current_len
+        count = max(0, seq_end - seq_start)
+        k = torch.empty((self.num_kv_heads, count, self.head_dim), dtype=self.dtype, device=self.device)
+        v = torch.empty_like(k)
+        self._call("lf_pool_read", self._meta_ref(), state.slot_id, layer, seq_start,
+                   seq_start + count, self.keys.data_ptr(), self.values.data_ptr(), k.data_ptr(),
+                   v.data_ptr(), self.num_layers, self.num_kv_heads, self.head_dim, self._stream())
+        return k, v
+
+    def read_all_layers(self, state: KVState, seq_start: int = 0,
+                        seq_end: Optional[int] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+        ks, vs = zip(*(self.read(state, l, seq_start, seq_end) for l in range(self.num_layers)))
+        return torch.stack(ks), torch.stack(vs)
+
+    def prefetch_next_slot(self, state: KVState) -> None:
+        """Kept for the executor's speculative-prefill hook (reference ``:189-198``).
+
+        The dense pool zeroed the next slot here.  Pages are never zeroed: a
+        session only reads positions below its length, so there is nothing to do.
+        """
+        return None
+
+    def hbm_usage_bytes(self) -> int:
+        meta = sum(t.numel() * 4 for t in (self._free_queue, self._refcount, self._table,
+                                            self._seq_len, self._ctrl, self._scratch))
+        return (self.keys.numel() + self.values.numel()) * self.keys.element_size() + meta
+
+    def stats(self) -> dict:
+        ctrl = self._ctrl.tolist()
+        return {
+            "hbm_mb": round(self.hbm_usage_bytes() / 1e6, 1),
+            "active_slots": len(self._active),
+            "free_slots": len(self._free_slots),
+            "writes": self._write_count,
+            "mb_written": round(self._bytes_written / 1e6, 1),
+            "pages_total": self.num_pages,
+            "pages_free": ctrl[_lib.LF_CTRL_COUNT],
+            "status": ctrl[_lib.LF_CTRL_STATUS],
+        }
+
+    def __repr__(self):
+        return (f"KVPool(layers={self.num_layers}, heads={self.num_heads}/{self.num_kv_heads}, "
+                f"dim={self.head_dim}, seq={self.max_seq_len}, slots={self.max_slots}, "
+                f"pages={self.num_pages})")
+
+    # -- paged API --------------------------------------------------------------
+    def alloc(self, n_tokens: int = 0) -> KVState:
+        """Open a session, optionally reserving pages for ``n_tokens`` (no data written)."""
+        st = self.allocate_slot()
+        if n_tokens:
+            self._reserve([st], [n_tokens])
+        return st
+
+    def _reserve(self, states: Sequence[KVState], counts: Sequence[int],
+                 stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        for s, n in zip(states, counts):
+            if s.current_len + n > self.max_seq_len:
+                raise RuntimeError(f"KV cache overflow: current_len={s.current_len} + "
+                                   f"seq_new={n} > max_seq_len={self.max_seq_len}")
+        ids = self._ids([s.slot_id for s in states])
+        cnt = self._ids(counts)
+        start = torch.empty(len(states), dtype=torch.int32, device=self.device)
+        self._call("lf_pool_reserve", self._meta_ref(), ids.data_ptr(), cnt.data_ptr(), len(states),
+                   start.data_ptr(), self._stream(stream))
+        if self._oversubscribed:
+            self._raise_if_failed("reserve")
+        for s, n in zip(states, counts):
+            s.current_len += n
+        return start
+
+    def append(self, states: Sequence[KVState], keys: Sequence[torch.Tensor],
+               values: Sequence[torch.Tensor], layout: str = "lthd",
+               stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Append new tokens to several sessions in one reserve + one scatter.
+
+        ``layout="lthd"``: each tensor is ``[L, T_i, Hkv, D]``; ``"lhsd"``: the
+        reference's ``[L, Hkv, T_i, D]``.  Tensors of one call share strides.
+        """
+        if len(states) == 0:
+            return
+        tdim = 1 if layout == "lthd" else 2
+        counts = [int(k.shape[tdim]) for k in keys]
+        start = self._reserve(states, counts, stream)
+        total = sum(counts)
+        if total == 0:
+            return
+        if len(keys) == 1:
+            k_all, v_all = keys[0], values[0]
+        else:
+            k_all = torch.cat(list(keys), dim=tdim)
+            v_all = torch.cat(list(values), dim=tdim)
+        for t in (k_all, v_all):
+            if t.device != self.device or t.dtype != self.dtype or t.stride(-1) != 1:
+                raise LoopfuseError(_lib.LF_EINVAL, "new K/V must be on the pool's device, in the "
+                                                    "pool dtype, with contiguous head_dim")
+        if v_all.stride() != k_all.stride():
+            v_all = v_all.contiguous()
+            k_all = k_all.contiguous()
+        sl = k_all.stride(0)
+        st_tok = k_all.stride(1) if layout == "lthd" else k_all.stride(2)
+        st_head = k_all.stride(2) if layout == "lthd" else k_all.stride(1)
+        cu = [0]
+        for c in counts:
+            cu.append(cu[-1] + c)
+        ids = self._ids([s.slot_id for s in states])
+        cu_t = self._ids(cu)
+        self._call("lf_pool_write_kv", self._meta_ref(), ids.data_ptr(), start.data_ptr(),
+                   cu_t.data_ptr(), len(states), total, k_all.data_ptr(), v_all.data_ptr(), sl,
+                   st_tok, st_head, self.keys.data_ptr(), self.values.data_ptr(), self.num_layers,
+                   self.num_kv_heads, self.head_dim, self._stream(stream))
+        self._write_count += 1
+        self._bytes_written += 2 * k_all.numel() * k_all.element_size()
+
+    def fork(self, state: KVState, prefix_len: Optional[int] = None, n: int = 1) -> List[KVState]:
+        """``n`` new sessions sharing ``state``'s first ``prefix_len`` tokens (KV fusion)."""
+        prefix_len = state.current_len if prefix_len is None else prefix_len
+        if prefix_len > state.current_len or prefix_len < 0:
+            raise LoopfuseError(_lib.LF_EINVAL, f"fork prefix {prefix_len} > length "
+                                                f"{state.current_len}")
+        if len(self._free_slots) < n:
+            raise RuntimeError(f"KVPool exhausted: all {self.max_slots} slots in use. "
+                               f"Increase max_slots or wait for a trajectory to complete.")
+        dsts = [self.allocate_slot() for _ in range(n)]
+        ids = self._ids([d.slot_id for d in dsts])
+        self._call("lf_pool_fork", self._meta_ref(), state.slot_id, ids.data_ptr(), n, prefix_len,
+                   self.keys.data_ptr(), self.values.data_ptr(), self.num_layers,
+                   self.num_kv_heads, self.head_dim, self._stream())
+        if self._oversubscribed and prefix_len % LF_PAGE_SIZE:
+            try:
+                self._raise_if_failed("fork")
+            except RuntimeError:
+                # nothing changed on the device: hand the slots back, first in line again
+                for d in dsts:
+                    del self._active[d.slot_id]
+                self._free_slots[0:0] = [d.slot_id for d in dsts]
+                raise
+        for d in dsts:
+            d.current_len = prefix_len
+        return dsts
+
+    def free(self, states: Union[KVState, Sequence[KVState]]) -> None:
+        """Drop the sessions' page references (slots stay allocated; see ``release``)."""
+        states = [states] if isinstance(states, KVState) else list(states)
+        if not states:
+            return
+        ids = self._ids([s.slot_id for s in states])
+        self._call("lf_pool_free", self._meta_ref(), ids.data_ptr(), len(states), self._stream())
+        for s in states:
+            s.current_len = 0
+
+    def release_all(self, states: Sequence[KVState]) -> None:
+        """Batched ``release``: one device free for all, slots back in the given order."""
+        states = [s for s in states if s.slot_id in self._active]
+        self.free(states)
+        for s in states:
+            del self._active[s.slot_id]
+            self._free_slots.append(s.slot_id)
+
+    def block_table(self, states: Sequence[KVState], max_pages: Optional[int] = None
+                    ) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Device ``[N, max_pages]`` int32 table and ``[N]`` lengths for ``paged_decode``."""
+        max_pages = max_pages or self.max_pages_per_seq
+        ids = self._ids([s.slot_id for s in states])
+        table = torch.empty((len(states), max_pages), dtype=torch.int32, device=self.device)
+        lens = torch.empty(len(states), dtype=torch.int32, device=self.device)
+        self._call("lf_pool_gather", self._meta_ref(), ids.data_ptr(), len(states),
+                   table.data_ptr(), max_pages, lens.data_ptr(), self._stream())
+        return table, lens
+
+    def layer_pages(self, layer: int) -> Tuple[torch.Tensor, torch.Tensor]:
+        """``[P, Hkv, 16, D]`` views of one layer's K and V pages."""
+        return self.keys[layer], self.values[layer]
+
+    def snapshot(self) -> dict:
+        """Host copy of the metadata (free queue from its head, refcounts, tables, lengths)."""
+        ctrl = self._ctrl.tolist()
+        head, count = ctrl[_lib.LF_CTRL_HEAD], ctrl[_lib.LF_CTRL_COUNT]
+        fq = self._free_queue.tolist()
+        P = self.num_pages
+        return {
+            "free_queue": [fq[(head + i) % P] for i in range(count)],
+            "refcount": self._refcount.tolist(),
+            "block_table": self._table.view(self.max_slots, self.max_pages_per_seq).tolist(),
+            "seq_len": self._seq_len.tolist(),
+            "status": ctrl[_lib.LF_CTRL_STATUS],
+        }

@@ -1,0 +1,49 @@
+"""The C-ABI library loads on a CPU host and exports every symbol the header declares.
+
+No compute call is made here (there is no GPU); only pure host-side entry points
+(version, workspace sizing, argument validation) are exercised.
+"""
+import ctypes
+import os
+import re
+
+import pytest
+
+from loopfuse_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include",
+                      "loopfuse_b200.h")
+
+
+def header_symbols():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(lf_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    syms = header_symbols()
+    assert len(syms) >= 12
+    for s in syms:
+        assert hasattr(lib, s), s
+    assert set(syms) == set(_lib.exported_symbols())
+
+
+def test_version_and_workspace_sizing():
+    assert _lib.lib().lf_version().startswith(b"loopfuse_b200")
+    n = ctypes.c_size_t(0)
+    _lib.call("lf_decode_workspace_size", 256, 32, 128, 2048, 32, 128, ctypes.byref(n))
+    slots = (2048 - 128 + 31) // 32 + 128 // 32
+    assert n.value == 256 * 32 * slots * (128 * 4 + 8)
+
+
+def test_host_side_validation_errors():
+    lib = _lib.lib()
+    rc = lib.lf_prefill_fwd(None, None, None, None, None, 1, 1, 1, 1, 1, 128, 1.0, 1, None)
+    assert rc == _lib.LF_EINVAL
+    assert b"null" in lib.lf_last_error()
+    rc = lib.lf_decode_fwd(8, 8, 8, 8, 8, 0, 8, None, 8, 0, 1, 4, 3, 128, 1, 1, 1, 1.0, None)
+    assert rc == _lib.LF_EINVAL          # unaligned pointers rejected before any launch
+    m = _lib.PoolMeta()
+    assert lib.lf_pool_init(ctypes.byref(m), None) == _lib.LF_EINVAL

@@ -1,0 +1,73 @@
+"""tcgen05 prefill (sm_100a) against the fp32 CPU oracle.
+
+Tolerance: bf16 output vs fp32 oracle, max-abs <= 2e-2 and mean-abs <= 2e-3;
+LSE (natural log) within 1e-2.
+"""
+import pytest
+import torch
+
+from oracle import attention as ora
+from loopfuse_b200 import attention as att
+from loopfuse_b200.workloads import prefill_inputs
+
+pytestmark = pytest.mark.gpu
+TOL_MAX, TOL_MEAN = 2e-2, 2e-3
+
+
+def _run_and_check(B, Hq, Hkv, Sq, Sk, causal, seed=0):
+    q, k, v = prefill_inputs(B, Hq, Hkv, Sq, 128, seed=seed, Sk=Sk)
+    o, lse = att.prefill_attention_fwd(q, k, v, causal=causal, return_lse=True)
+    ref, ref_lse = ora.prefill(q.cpu(), k.cpu(), v.cpu(), causal=causal)
+    d = (o.float().cpu() - ref).abs()
+    assert d.max().item() <= TOL_MAX, d.max().item()
+    assert d.mean().item() <= TOL_MEAN, d.mean().item()
+    fin = torch.isfinite(ref_lse)
+    assert torch.equal(torch.isfinite(lse.cpu()), fin)
+    assert (lse.cpu()[fin] - ref_lse[fin]).abs().max().item() < 1e-2
+
+
+@pytest.mark.parametrize("S", [128, 256, 512])
+def test_prefill_causal_mha(S):
+    _run_and_check(1, 2, 2, S, S, True)
+
+
+@pytest.mark.parametrize("S", [1, 17, 129, 200, 383])
+def test_prefill_ragged_lengths(S):
+    _run_and_check(2, 4, 1, S, S, True, seed=S)
+
+
+def test_prefill_gqa_noncausal():
+    _run_and_check(1, 8, 2, 256, 384, False, seed=3)
+
+
+@pytest.mark.parametrize("Sq,Sk", [(128, 384), (40, 300), (256, 257)])
+def test_prefill_appended_queries(Sq, Sk):
+    """Bottom-right causal: new tool-output tokens attend to a cached prefix."""
+    _run_and_check(1, 4, 1, Sq, Sk, True, seed=Sq + Sk)
+
+
+def test_prefill_longer_sequence():
+    _run_and_check(1, 8, 2, 1024, 1024, True, seed=11)
+
+
+def test_prefill_full_size_sampled():
+    """B=8, Hq=32, Hkv=8, S=4096: one GQA group of batch 5 checked against the oracle,
+    and determinism of the full launch."""
+    q, k, v = prefill_inputs(seed=0)
+    o = att.prefill_attention_fwd(q, k, v, causal=True)
+    o2 = att.prefill_attention_fwd(q, k, v, causal=True)
+    assert torch.equal(o, o2)
+    b, g = 5, 3
+    ref, _ = ora.prefill(q[b:b + 1, 4 * g:4 * g + 4].cpu(), k[b:b + 1, g:g + 1].cpu(),
+                         v[b:b + 1, g:g + 1].cpu(), causal=True)
+    d = (o[b:b + 1, 4 * g:4 * g + 4].float().cpu() - ref).abs()
+    assert d.max().item() <= TOL_MAX and d.mean().item() <= TOL_MEAN
+    assert torch.isfinite(o.float()).all()
+
+
+def test_prefill_reference_api_shape_and_dtype_checks():
+    q, k, v = prefill_inputs(1, 2, 2, 64, 128, seed=1)
+    with pytest.raises(RuntimeError):
+        att.prefill_attention_fwd(q.float(), k, v)
+    with pytest.raises(RuntimeError):
+        att.prefill_attention_fwd(q, k[:, :, :, :64].contiguous(), v)
