@@ -268,6 +268,10 @@ def main():
     stream = torch.cuda.current_stream()
     split_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                 for _ in range(K)]
+    for a, b in split_ev:          # torch creates the CUDA event on first record
+        a.record(stream)
+        b.record(stream)
+    torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     lib = _lib.lib()
     with ClockSampler(uuid) as clk:

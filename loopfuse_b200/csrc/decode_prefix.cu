@@ -10,9 +10,9 @@
 // directly to the slot suffix_splits + chunk; the combine kernel merges it with the
 // session's own splits.
 //
-// The page ids are read from the group's first session; callers guarantee the prefix
-// entries are equal across sessions (KVPool.fork produces exactly that).  Tokens at or past a
-// session's length are masked, so a session shorter than the prefix is still exact.
+// The page ids are read from the group's longest session; callers guarantee the prefix
+// entries a session holds equal everybody else's (KVPool.fork produces exactly that).  Tokens
+// at or past a session's length are masked, so a session shorter than the prefix is exact.
 #include "decode_common.cuh"
 
 #include <math.h>
@@ -49,8 +49,22 @@ prefix_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kp,
     __shared__ __align__(16) uint4 sk[kVec];
     __shared__ __align__(16) uint4 sv[kVec];
 
+    // Page ids come from the group's longest session: every session's row holds the shared
+    // pages it covers, and the longest one covers all the pages any session here needs.
     const int n0 = grp * PrefixCfg<G>::SPC;
-    const int32_t* bt_row = bt + (size_t)n0 * max_pages;
+    __shared__ int s_src, s_src_pages;
+    if (threadIdx.x == 0) {
+        int best = n0, best_len = -1;
+        for (int n = n0; n < min(n0 + PrefixCfg<G>::SPC, N); ++n) {
+            const int L = min(max(seq_lens[n], 0), max_pages * kPage);
+            if (L > best_len) { best_len = L; best = n; }
+        }
+        s_src = best;
+        s_src_pages = (max(best_len, 0) + kPage - 1) / kPage;
+    }
+    __syncthreads();
+    const int32_t* bt_row = bt + (size_t)s_src * max_pages;
+    const int p_stop = min(p_end, s_src_pages);
 
     int sess[SPW], len[SPW];
     float qf[SPW][G][8], acc[SPW][G][8], m_run[SPW], l_run[SPW];
@@ -93,9 +107,9 @@ prefix_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kp,
             }
         }
     };
-    if (p_begin < p_end) fetch(p_begin);
+    if (p_begin < p_stop) fetch(p_begin);
 
-    for (int pi = p_begin; pi < p_end; ++pi) {
+    for (int pi = p_begin; pi < p_stop; ++pi) {
 #pragma unroll
         for (int e = 0; e < kPer; ++e) {
             const int idx = threadIdx.x + e * kThreads;
@@ -105,7 +119,7 @@ prefix_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kp,
             }
         }
         __syncthreads();
-        if (pi + 1 < p_end) fetch(pi + 1);
+        if (pi + 1 < p_stop) fetch(pi + 1);
 
 #pragma unroll
         for (int i = 0; i < SPW; ++i) {
