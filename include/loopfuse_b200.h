@@ -96,6 +96,25 @@ int lf_decode_fwd(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* v_pag
                   int num_pages, int max_pages, int pages_per_split, float scale,
                   void* stream);
 
+/* Decode without any device allocation.  Same computation as lf_decode_fwd,
+ * but the split partials live in a fixed array inside the library
+ * (LF_DECODE_NOALLOC_SCRATCH_BYTES on every GPU that loads it, held until
+ * exit), so callers that cannot allocate device memory -- a foreign-language
+ * binding without a device allocator, or a loop whose allocator has reserved
+ * nearly all of HBM for the KV pool -- need pass only inputs and outputs.
+ * No counterpart in the reference.  The split size is chosen internally to
+ * fit the array; a request that does not fit even with one split per session
+ * returns LF_EINVAL.  The first call on a device looks up the array's device
+ * address (with that device current), so make it before any stream capture.
+ * Calls share the array: calls whose kernels overlap on the GPU race and must
+ * be serialised by the caller. */
+#define LF_DECODE_NOALLOC_SCRATCH_BYTES (32u << 20)
+int lf_decode_fwd_noalloc(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* v_pages,
+                          const int32_t* block_table, const int32_t* seq_lens,
+                          int num_prefix_pages, lf_bf16* o, float* lse, int num_seqs,
+                          int num_q_heads, int num_kv_heads, int head_dim, int num_pages,
+                          int max_pages, float scale, void* stream);
+
 /* Instrumentation for timing the dominant decode kernel: while both events
  * are non-null, every lf_decode_fwd records ev_begin right before and ev_end
  * right after its per-session split kernel, on the call's stream (events are

@@ -43,6 +43,8 @@ _SIGS = {
     "lf_decode_workspace_size": [c_int, c_int, c_int, c_int, c_int, c_int, POINTER(c_size_t)],
     "lf_decode_fwd": [_P, _P, _P, _P, _P, c_int, _P, _P, _P, c_size_t, c_int, c_int, c_int,
                       c_int, c_int, c_int, c_int, c_float, _P],
+    "lf_decode_fwd_noalloc": [_P, _P, _P, _P, _P, c_int, _P, _P, c_int, c_int, c_int, c_int,
+                              c_int, c_int, c_float, _P],
     "lf_decode_set_profile_events": [_P, _P],
     "lf_pool_init": [POINTER(PoolMeta), _P],
     "lf_pool_clear_status": [POINTER(PoolMeta), _P],

@@ -355,3 +355,133 @@ extern "C" int lf_decode_fwd(const lf_bf16* q, const lf_bf16* k_pages, const lf_
                                                          n_slots, max_split, n_prefix_chunks);
     return launch_status("decode combine");
 }
+
+// ---- decode without device allocation ------------------------------------------------------
+//
+// lf_decode_fwd needs a caller-provided workspace for the split partials.  Some callers have
+// no way to provide one: a binding from another language with no device allocator of its own,
+// or a serving loop whose caching allocator has already reserved nearly all of HBM for the KV
+// pool, where a cudaMalloc would fail or synchronise the device.  lf_decode_fwd_noalloc runs
+// the same kernels with the partials kept in the fixed array below, which is part of the
+// library image: every GPU that loads the library holds these bytes until the process exits.
+//
+// The split size is chosen here (the smallest power-of-two page count, from the default
+// heuristic upward, whose partials fit); a request whose partials do not fit even with one
+// split per session is rejected with LF_EINVAL.  Every slot the combine kernel reads is written
+// earlier in the same call, so nothing in the array needs clearing between calls.  All calls
+// share the array: two calls whose kernels overlap on the GPU (different streams, or different
+// host threads on one device) race on it and must be serialised by the caller.
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[LF_DECODE_NOALLOC_SCRATCH_BYTES];
+
+#include <mutex>
+
+namespace lf {
+namespace decode {
+
+// Device address of g_noalloc_scratch on the current device.  The symbol's host-side name is
+// only a stand-in, so the address is looked up once per device (the first call on a device does
+// this, with that device current) and cached.
+static int noalloc_scratch(void** out) {
+    static std::mutex mu;
+    static void* addr[128] = {nullptr};
+    int dev = 0;
+    LF_CHECK_CUDA(cudaGetDevice(&dev));
+    LF_CHECK_ARG(dev >= 0 && dev < 128, "decode noalloc: device ordinal %d out of range", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (addr[dev] == nullptr) {
+        void* p = nullptr;
+        LF_CHECK_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return LF_OK;
+}
+
+static size_t partial_bytes(int N, int Hq, int D, int max_pages, int pps, int n_prefix) {
+    return (size_t)N * Hq * (size_t)num_slots(max_pages, pps, n_prefix) *
+           ((size_t)D * sizeof(float) + sizeof(float2));
+}
+
+}  // namespace decode
+}  // namespace lf
+
+extern "C" int lf_decode_fwd_noalloc(const lf_bf16* q, const lf_bf16* k_pages,
+                                     const lf_bf16* v_pages, const int32_t* block_table,
+                                     const int32_t* seq_lens, int num_prefix_pages, lf_bf16* o,
+                                     float* lse, int num_seqs, int num_q_heads, int num_kv_heads,
+                                     int head_dim, int num_pages, int max_pages, float scale,
+                                     void* stream) {
+    LF_CHECK_ARG(q && k_pages && v_pages && block_table && seq_lens && o,
+                 "decode noalloc: null pointer argument");
+    LF_CHECK_ARG(aligned16(q) && aligned16(k_pages) && aligned16(v_pages) && aligned16(o),
+                 "decode noalloc: q, pages and o must be 16-byte aligned");
+    LF_CHECK_ARG(head_dim == 128 || head_dim == 64, "decode noalloc: head_dim must be 64 or 128");
+    LF_CHECK_ARG(num_seqs > 0 && num_seqs <= 65535 && num_kv_heads > 0 && num_kv_heads <= 65535 &&
+                     num_q_heads % num_kv_heads == 0,
+                 "decode noalloc: need 0 < num_seqs <= 65535 and Hq a multiple of Hkv");
+    LF_CHECK_ARG(num_pages > 0 && max_pages > 0 && num_prefix_pages >= 0 &&
+                     num_prefix_pages <= max_pages,
+                 "decode noalloc: bad page counts");
+
+    // Split size: the default heuristic, doubled until the partials fit the fixed scratch.
+    long per = (long)num_seqs * num_kv_heads * max_pages / (148L * 3 * 8);
+    int pps = 8;
+    while (pps < per && pps < 128) pps *= 2;
+    while (decode::partial_bytes(num_seqs, num_q_heads, head_dim, max_pages, pps, num_prefix_pages) >
+               (size_t)LF_DECODE_NOALLOC_SCRATCH_BYTES &&
+           pps < max_pages)
+        pps = pps * 2 < max_pages ? pps * 2 : max_pages;
+    const size_t need =
+        decode::partial_bytes(num_seqs, num_q_heads, head_dim, max_pages, pps, num_prefix_pages);
+    LF_CHECK_ARG(need <= (size_t)LF_DECODE_NOALLOC_SCRATCH_BYTES,
+                 "decode noalloc: %d sessions x %d heads need %zu bytes of partials even with one "
+                 "split per session; the fixed scratch holds %u bytes (use lf_decode_fwd with a "
+                 "workspace)",
+                 num_seqs, num_q_heads, need, (unsigned)LF_DECODE_NOALLOC_SCRATCH_BYTES);
+
+    void* scratch = nullptr;
+    int rc = decode::noalloc_scratch(&scratch);
+    if (rc != LF_OK) return rc;
+
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int G = num_q_heads / num_kv_heads;
+    const int n_slots = decode::num_slots(max_pages, pps, num_prefix_pages);
+    const int max_split = decode::suffix_splits(max_pages, pps, num_prefix_pages);
+    const int n_prefix_chunks = decode::prefix_chunks(pps, num_prefix_pages);
+    float* po = static_cast<float*>(scratch);
+    float2* pml = reinterpret_cast<float2*>(po + (size_t)num_seqs * num_q_heads * n_slots * head_dim);
+    const float qscale = scale * kLog2e;
+
+    if (num_prefix_pages > 0) {
+        rc = decode::launch_prefix(q, k_pages, v_pages, block_table, seq_lens, po, pml, num_seqs,
+                                   num_q_heads, num_kv_heads, head_dim, num_pages, max_pages,
+                                   num_prefix_pages, pps, n_slots, max_split, qscale, st);
+        if (rc != LF_OK) return rc;
+    }
+    if (max_split > 0) {
+        dim3 grid(max_split, num_kv_heads, num_seqs);
+        rc = head_dim == 128
+                 ? decode::dispatch_group<128>(G, grid, st, q, k_pages, v_pages, block_table,
+                                               seq_lens, po, pml, num_q_heads, num_kv_heads,
+                                               num_pages, max_pages, pps, num_prefix_pages,
+                                               n_slots, qscale)
+                 : decode::dispatch_group<64>(G, grid, st, q, k_pages, v_pages, block_table,
+                                              seq_lens, po, pml, num_q_heads, num_kv_heads,
+                                              num_pages, max_pages, pps, num_prefix_pages,
+                                              n_slots, qscale);
+        if (rc != LF_OK) return rc;
+        rc = launch_status("decode noalloc split");
+        if (rc != LF_OK) return rc;
+    }
+    dim3 cgrid(num_q_heads, num_seqs);
+    if (head_dim == 128)
+        decode::combine_kernel<128><<<cgrid, 32, 0, st>>>(po, pml, seq_lens, o, lse, num_q_heads,
+                                                          max_pages, pps, num_prefix_pages,
+                                                          n_slots, max_split, n_prefix_chunks);
+    else
+        decode::combine_kernel<64><<<cgrid, 16, 0, st>>>(po, pml, seq_lens, o, lse, num_q_heads,
+                                                         max_pages, pps, num_prefix_pages,
+                                                         n_slots, max_split, n_prefix_chunks);
+    return launch_status("decode noalloc combine");
+}
