@@ -240,7 +240,13 @@ int dispatch_group(int G, dim3 grid, cudaStream_t st, const uint16_t* q, const u
 inline int suffix_splits(int max_pages, int pps, int n_prefix) {
     return (max_pages - n_prefix + pps - 1) / pps;
 }
-inline int prefix_chunks(int pps, int n_prefix) { return (n_prefix + pps - 1) / pps; }
+// Shared-prefix pages are cut into chunks of at most 32 pages (one tensor-core CTA each) so the
+// prefix pass fills the GPU even when sessions use long splits.
+inline int prefix_chunk_pages(int pps) { return pps < 32 ? pps : 32; }
+inline int prefix_chunks(int pps, int n_prefix) {
+    const int c = prefix_chunk_pages(pps);
+    return (n_prefix + c - 1) / c;
+}
 inline int num_slots(int max_pages, int pages_per_split, int num_prefix_pages) {
     return suffix_splits(max_pages, pages_per_split, num_prefix_pages) +
            prefix_chunks(pages_per_split, num_prefix_pages);
@@ -321,7 +327,7 @@ extern "C" int lf_decode_fwd(const lf_bf16* q, const lf_bf16* k_pages, const lf_
     if (num_prefix_pages > 0) {
         int rc = decode::launch_prefix(q16, k_pages, v_pages, block_table, seq_lens, po, pml,
                                        num_seqs, num_q_heads, num_kv_heads, head_dim, num_pages,
-                                       max_pages, num_prefix_pages, pages_per_split, n_slots, max_split,
+                                       max_pages, num_prefix_pages, decode::prefix_chunk_pages(pages_per_split), n_slots, max_split,
                                        qscale, st);
         if (rc != LF_OK) return rc;
     }
@@ -456,7 +462,8 @@ extern "C" int lf_decode_fwd_noalloc(const lf_bf16* q, const lf_bf16* k_pages,
     if (num_prefix_pages > 0) {
         rc = decode::launch_prefix(q, k_pages, v_pages, block_table, seq_lens, po, pml, num_seqs,
                                    num_q_heads, num_kv_heads, head_dim, num_pages, max_pages,
-                                   num_prefix_pages, pps, n_slots, max_split, qscale, st);
+                                   num_prefix_pages, decode::prefix_chunk_pages(pps), n_slots, max_split,
+                                   qscale, st);
         if (rc != LF_OK) return rc;
     }
     if (max_split > 0) {

@@ -5,10 +5,6 @@
 #include "lf_common.cuh"
 
 namespace lf {
-extern __device__ int g_device_error;
-}
-
-namespace lf {
 namespace decode {
 
 constexpr int kPage = LF_PAGE_SIZE;

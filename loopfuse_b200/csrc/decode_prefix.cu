@@ -232,10 +232,20 @@ static int dispatch_prefix(int G, dim3 grid, cudaStream_t st, const uint16_t* q,
     return launch_status("decode prefix");
 }
 
+// Tensor-core version (head_dim 128), in prefill.cu.
+int launch_prefix_tc(const uint16_t* q, const uint16_t* kp, const uint16_t* vp, const int32_t* bt,
+                     const int32_t* lens, float* po, float2* pml, int N, int Hq, int Hkv,
+                     int num_pages, int max_pages, int n_prefix, int chunk_pages, int n_slots,
+                     int slot0, float qscale, cudaStream_t st);
+
+// head_dim 128 runs on the tensor cores; head_dim 64 on the CUDA-core kernel above.
 int launch_prefix(const uint16_t* q, const uint16_t* kp, const uint16_t* vp, const int32_t* bt,
                   const int32_t* lens, float* po, float2* pml, int N, int Hq, int Hkv, int D,
                   int num_pages, int max_pages, int n_prefix, int pages_per_chunk, int n_slots,
                   int slot0, float qscale, cudaStream_t st) {
+    if (D == 128)
+        return launch_prefix_tc(q, kp, vp, bt, lens, po, pml, N, Hq, Hkv, num_pages, max_pages,
+                                n_prefix, pages_per_chunk, n_slots, slot0, qscale, st);
     const int G = Hq / Hkv;
     const int spc = G >= 8 ? PrefixCfg<8>::SPC : PrefixCfg<1>::SPC;
     dim3 grid((n_prefix + pages_per_chunk - 1) / pages_per_chunk, Hkv, (N + spc - 1) / spc);

@@ -70,4 +70,25 @@ __device__ __forceinline__ float fast_exp2(float x) {
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
+// Device-side error reporting.  Each translation unit gets its own error word (device code is
+// compiled per unit, without cross-unit device linking); a kernel whose bounded wait gave up,
+// or that met a bad page id, stores a site code there instead of faulting or hanging.  Each
+// unit registers a reader at load time, and lf_device_status() collects and clears them all.
+using DeviceErrorReader = int (*)();
+bool register_device_error_reader(DeviceErrorReader fn);
+
+static __device__ int g_device_error = 0;
+
+static int take_device_error() {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)) != cudaSuccess) return -1;
+    if (v != 0) {
+        const int zero = 0;
+        cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+    }
+    return v;
+}
+
+static const bool g_device_error_registered = register_device_error_reader(&take_device_error);
+
 }  // namespace lf
