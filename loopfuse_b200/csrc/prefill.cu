@@ -3,11 +3,11 @@
 // Replaces prefill_attention_fwd (kernels/triton/prefill_attn.py:127-168, an FA2-style
 // Triton kernel, MHA/fp16 only) and the reference's sm_80 agent_prefill_kernel
 // (kernels/cuda/async_prefill.cu:56-236, wmma QK^T only, no softmax or P.V).  The kernel is the
-// dense instantiation of the tcgen05 attention core in attn_tc.cuh: one CTA per 128-row query
-// tile of one (batch, query head), heavy (far-from-diagonal) tiles launched first.
+// dense instantiation of the tcgen05 attention core in attn_tc2.cuh: one CTA per pair of
+// adjacent 128-row query tiles of one (batch, query head), heavy pairs launched first.
 //
 // This file also launches the core's Prefix instantiation for the decode's shared-prefix pass.
-#include "attn_tc.cuh"
+#include "attn_tc2.cuh"
 #include "tmap.cuh"
 
 using namespace lf;
@@ -15,7 +15,7 @@ using namespace lf;
 extern "C" int lf_prefill_fwd(const lf_bf16* q, const lf_bf16* k, const lf_bf16* v, lf_bf16* o,
                               float* lse, int batch, int num_q_heads, int num_kv_heads, int seq_q,
                               int seq_k, int head_dim, float scale, int causal, void* stream) {
-    using namespace lf::tc;
+    using namespace lf::tc2;
     LF_CHECK_ARG(q && k && v && o, "prefill: null pointer argument");
     LF_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o),
                  "prefill: q, k, v, o must be 16-byte aligned");
@@ -24,7 +24,8 @@ extern "C" int lf_prefill_fwd(const lf_bf16* q, const lf_bf16* k, const lf_bf16*
                  "prefill: need Hq a positive multiple of Hkv");
     LF_CHECK_ARG(seq_q > 0 && seq_k > 0, "prefill: sequence lengths must be positive");
     const long n_qt = (seq_q + BM - 1) / BM;
-    const long grid = n_qt * batch * num_q_heads;
+    const long n_pairs = (n_qt + 1) / 2;
+    const long grid = n_pairs * batch * num_q_heads;
     LF_CHECK_ARG(grid < 2147483647L, "prefill: grid too large");
 
     // [B*H][S][128] bf16 views; [128 rows][64 dims] boxes.
@@ -43,7 +44,7 @@ extern "C" int lf_prefill_fwd(const lf_bf16* q, const lf_bf16* k, const lf_bf16*
 
     static bool attr_set = false;
     if (!attr_set) {
-        LF_CHECK_CUDA(cudaFuncSetAttribute(attn_kernel<Mode::Dense>,
+        LF_CHECK_CUDA(cudaFuncSetAttribute(attn2_kernel<Mode::Dense>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
         attr_set = true;
     }
@@ -57,9 +58,10 @@ extern "C" int lf_prefill_fwd(const lf_bf16* q, const lf_bf16* k, const lf_bf16*
     p.Sq = seq_q;
     p.Sk = seq_k;
     p.n_qt = (int)n_qt;
+    p.n_pairs = (int)n_pairs;
     p.causal = causal ? 1 : 0;
     p.q_offset = seq_k - seq_q;
-    attn_kernel<Mode::Dense><<<(unsigned)grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
+    attn2_kernel<Mode::Dense><<<(unsigned)grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
         mq, mk, mv, p);
     return launch_status("prefill");
 }
@@ -68,13 +70,13 @@ namespace lf {
 namespace decode {
 
 // Shared-prefix partials on the tensor cores (head_dim 128): the Prefix instantiation of the
-// attention core.  Query rows are 128/G sessions x G heads of one KV head; each CTA covers one
-// chunk of prefix pages and writes fp32 partials to workspace slots slot0 + chunk.
+// attention core.  Each CTA takes 2 x 128 query rows = 256/G sessions x G heads of one KV head
+// and one chunk of prefix pages, and writes fp32 partials to workspace slots slot0 + chunk.
 int launch_prefix_tc(const uint16_t* q, const uint16_t* kp, const uint16_t* vp, const int32_t* bt,
                      const int32_t* lens, float* po, float2* pml, int N, int Hq, int Hkv,
                      int num_pages, int max_pages, int n_prefix, int chunk_pages, int n_slots,
                      int slot0, float qscale, cudaStream_t st) {
-    using namespace lf::tc;
+    using namespace lf::tc2;
     const int G = Hq / Hkv;
     LF_CHECK_ARG(G >= 1 && G <= 8 && (G & (G - 1)) == 0, "decode prefix: Hq/Hkv must be 1, 2, 4 or 8");
     CUtensorMap mq, mk, mv;
@@ -95,7 +97,7 @@ int launch_prefix_tc(const uint16_t* q, const uint16_t* kp, const uint16_t* vp, 
 
     static bool attr_set = false;
     if (!attr_set) {
-        LF_CHECK_CUDA(cudaFuncSetAttribute(attn_kernel<Mode::Prefix>,
+        LF_CHECK_CUDA(cudaFuncSetAttribute(attn2_kernel<Mode::Prefix>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
         attr_set = true;
     }
@@ -113,12 +115,12 @@ int launch_prefix_tc(const uint16_t* q, const uint16_t* kp, const uint16_t* vp, 
     p.n_prefix = n_prefix;
     p.chunk_pages = chunk_pages;
     p.n_chunks = (n_prefix + chunk_pages - 1) / chunk_pages;
-    p.n_qtiles = (N * G + BM - 1) / BM;
+    p.n_qtiles = (N * G + 2 * BM - 1) / (2 * BM);
     p.n_slots = n_slots;
     p.slot0 = slot0;
     const long grid = (long)p.n_qtiles * Hkv * p.n_chunks;
     LF_CHECK_ARG(grid < 2147483647L, "decode prefix: grid too large");
-    attn_kernel<Mode::Prefix><<<(unsigned)grid, kThreads, kSmemBytes, st>>>(mq, mk, mv, p);
+    attn2_kernel<Mode::Prefix><<<(unsigned)grid, kThreads, kSmemBytes, st>>>(mq, mk, mv, p);
     return launch_status("decode prefix (tensor cores)");
 }
 

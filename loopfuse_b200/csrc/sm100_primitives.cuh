@@ -92,6 +92,55 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+// ---- packed fp32 pairs (sm_100a f32x2 arithmetic) -------------------------------------------
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ float2 f2_unpack(uint64_t v) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// 2^t for a pair of inputs on the FMA pipe, to take part of the exponentials off the MUFU unit.
+// Method: Cody-Waite style range reduction t = j + f, j = round-to-nearest(t) obtained by adding
+// and subtracting 1.5*2^23, f in [-0.5, 0.5]; 2^f by a degree-3 polynomial with p(0) = 1 whose
+// other coefficients were fitted for minimax relative error on [-0.5, 0.5] (Lawson-weighted
+// least squares); 2^j is added to the exponent field.  Max relative error 1.0e-4 on [-125, 8]
+// (below the 2^-9 rounding of the bf16 probabilities it feeds); inputs <= -127, including -inf,
+// give exactly 0.
+constexpr float kExp2C1 = 0.6932829022407532f;
+constexpr float kExp2C2 = 0.2422109693288803f;
+constexpr float kExp2C3 = 0.05500892922282219f;
+
+__device__ __forceinline__ float2 exp2_poly2(uint64_t t2) {
+    float2 t = f2_unpack(t2);
+    t.x = fmaxf(t.x, -127.f);
+    t.y = fmaxf(t.y, -127.f);
+    const uint64_t tc = f2_pack(t.x, t.y);
+    const uint64_t y = fadd2(tc, f2_pack(12582912.f, 12582912.f));        // round(t) in low bits
+    const uint64_t jf = fadd2(y, f2_pack(-12582912.f, -12582912.f));      // round(t) as float
+    const uint64_t fr = ffma2(jf, f2_pack(-1.f, -1.f), tc);               // t - round(t)
+    uint64_t pp = ffma2(f2_pack(kExp2C3, kExp2C3), fr, f2_pack(kExp2C2, kExp2C2));
+    pp = ffma2(pp, fr, f2_pack(kExp2C1, kExp2C1));
+    pp = ffma2(pp, fr, f2_pack(1.f, 1.f));
+    const float2 pv = f2_unpack(pp), yv = f2_unpack(y);
+    return make_float2(__int_as_float(__float_as_int(pv.x) + (__float_as_int(yv.x) << 23)),
+                       __int_as_float(__float_as_int(pv.y) + (__float_as_int(yv.y) << 23)));
+}
+
 // ---- tcgen05 ----------------------------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t slot_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot_smem),
