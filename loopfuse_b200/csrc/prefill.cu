@@ -3,8 +3,8 @@
 // Replaces prefill_attention_fwd (kernels/triton/prefill_attn.py:127-168, an FA2-style
 // Triton kernel, MHA/fp16 only) and the reference's sm_80 agent_prefill_kernel
 // (kernels/cuda/async_prefill.cu:56-236, wmma QK^T only, no softmax or P.V).  The kernel is the
-// dense instantiation of the tcgen05 attention core in attn_tc2.cuh: one CTA per pair of
-// adjacent 128-row query tiles of one (batch, query head), heavy pairs launched first.
+// dense instantiation of the tcgen05 attention core in attn_tc2.cuh: persistent CTAs (one per
+// SM) walk pairs of adjacent 128-row query tiles of one (batch, query head), heavy pairs first.
 //
 // This file also launches the core's Prefix instantiation for the decode's shared-prefix pass.
 #include "attn_tc2.cuh"
@@ -25,8 +25,11 @@ extern "C" int lf_prefill_fwd(const lf_bf16* q, const lf_bf16* k, const lf_bf16*
     LF_CHECK_ARG(seq_q > 0 && seq_k > 0, "prefill: sequence lengths must be positive");
     const long n_qt = (seq_q + BM - 1) / BM;
     const long n_pairs = (n_qt + 1) / 2;
-    const long grid = n_pairs * batch * num_q_heads;
-    LF_CHECK_ARG(grid < 2147483647L, "prefill: grid too large");
+    const long n_items = n_pairs * batch * num_q_heads;
+    LF_CHECK_ARG(n_items < 2147483647L, "prefill: too many query tiles");
+    int sms = 0;
+    LF_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0));
+    const long grid = n_items < sms ? n_items : sms;   // persistent: one CTA per SM
 
     // [B*H][S][128] bf16 views; [128 rows][64 dims] boxes.
     CUtensorMap mq, mk, mv;
@@ -59,6 +62,7 @@ extern "C" int lf_prefill_fwd(const lf_bf16* q, const lf_bf16* k, const lf_bf16*
     p.Sk = seq_k;
     p.n_qt = (int)n_qt;
     p.n_pairs = (int)n_pairs;
+    p.n_items = (int)n_items;
     p.causal = causal ? 1 : 0;
     p.q_offset = seq_k - seq_q;
     attn2_kernel<Mode::Dense><<<(unsigned)grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
@@ -118,8 +122,12 @@ int launch_prefix_tc(const uint16_t* q, const uint16_t* kp, const uint16_t* vp, 
     p.n_qtiles = (N * G + 2 * BM - 1) / (2 * BM);
     p.n_slots = n_slots;
     p.slot0 = slot0;
-    const long grid = (long)p.n_qtiles * Hkv * p.n_chunks;
-    LF_CHECK_ARG(grid < 2147483647L, "decode prefix: grid too large");
+    const long n_items = (long)p.n_qtiles * Hkv * p.n_chunks;
+    LF_CHECK_ARG(n_items < 2147483647L, "decode prefix: too many work items");
+    p.n_items = (int)n_items;
+    int sms = 0;
+    LF_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0));
+    const long grid = n_items < sms ? n_items : sms;
     attn2_kernel<Mode::Prefix><<<(unsigned)grid, kThreads, kSmemBytes, st>>>(mq, mk, mv, p);
     return launch_status("decode prefix (tensor cores)");
 }
