@@ -71,6 +71,23 @@ int lf_prefill_fwd(const lf_bf16* q, const lf_bf16* k, const lf_bf16* v, lf_bf16
                    float* lse, int batch, int num_q_heads, int num_kv_heads, int seq_q,
                    int seq_k, int head_dim, float scale, int causal, void* stream);
 
+/* Prefill over cached paged context (tool-output appends).  Extends the same
+ * reference entry points to queries appended after a session's cached KV:
+ * q [total_q, Hq, D] holds the new tokens of num_seqs sessions back to back
+ * (session n owns rows cu_seqlens_q[n] .. cu_seqlens_q[n+1]-1, at most
+ * max_seqlen_q of them); its keys and values are the first seqlens_k[n] tokens
+ * of its block-table row in the pool pages [P, Hkv, 16, D] (the new tokens
+ * already written).  causal != 0 puts query i of session n at key position
+ * seqlens_k[n] - (its query count) + i.  o [total_q, Hq, D]; lse [total_q, Hq]
+ * (nullable).  The reference's causal mask assumes seq_q == seq_k
+ * (kernels/triton/prefill_attn.py:98) and has no cached-prefix prefill. */
+int lf_prefill_paged_fwd(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* v_pages,
+                         const int32_t* block_table, const int32_t* cu_seqlens_q,
+                         const int32_t* seqlens_k, lf_bf16* o, float* lse, int num_seqs,
+                         int total_q, int max_seqlen_q, int num_q_heads, int num_kv_heads,
+                         int head_dim, int num_pages, int max_pages, float scale, int causal,
+                         void* stream);
+
 /* ---- paged split-KV decode ----------------------------------------------
  * Replaces decode_attention_fwd (kernels/triton/decode_attn.py:133-171) and
  * ring_kv_decode_kernel (kernels/cuda/ring_kv_cache.cu:120-248).

@@ -40,6 +40,8 @@ _SIGS = {
     "lf_device_status": [POINTER(c_int)],
     "lf_prefill_fwd": [_P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, c_int, c_float,
                        c_int, _P],
+    "lf_prefill_paged_fwd": [_P, _P, _P, _P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int,
+                             c_int, c_int, c_int, c_float, c_int, _P],
     "lf_decode_workspace_size": [c_int, c_int, c_int, c_int, c_int, c_int, POINTER(c_size_t)],
     "lf_decode_fwd": [_P, _P, _P, _P, _P, c_int, _P, _P, _P, c_size_t, c_int, c_int, c_int,
                       c_int, c_int, c_int, c_int, c_float, _P],

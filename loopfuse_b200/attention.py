@@ -59,6 +59,38 @@ def prefill_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cau
     return (o, lse) if return_lse else o
 
 
+def prefill_paged(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torch.Tensor,
+                  block_table: torch.Tensor, cu_seqlens_q: torch.Tensor, seqlens_k: torch.Tensor,
+                  max_seqlen_q: int, causal: bool = True, scale: Optional[float] = None,
+                  return_lse: bool = False):
+    """Attention of newly appended tokens over each session's cached paged K/V.
+
+    ``q [T, Hq, D]``: the new tokens of N sessions back to back, session ``n`` owning rows
+    ``cu_seqlens_q[n] .. cu_seqlens_q[n+1]``; ``k_pages, v_pages [P, Hkv, 16, D]`` (one layer,
+    new tokens already appended); ``block_table [N, max_pages]``; ``seqlens_k [N]`` context
+    lengths including the new tokens.  Causal with the queries at the end of their session.
+    Returns ``o [T, Hq, D]`` (and ``lse [T, Hq]``).
+    """
+    for t, n in ((q, "q"), (k_pages, "k_pages"), (v_pages, "v_pages")):
+        _require(t, n)
+    for t, n in ((block_table, "block_table"), (cu_seqlens_q, "cu_seqlens_q"),
+                 (seqlens_k, "seqlens_k")):
+        _require(t, n, torch.int32)
+    T, Hq, D = q.shape
+    P, Hkv, page, Dk = k_pages.shape
+    N = block_table.shape[0]
+    if page != LF_PAGE_SIZE or Dk != D or cu_seqlens_q.shape != (N + 1,) or seqlens_k.shape != (N,):
+        raise LoopfuseError(_lib.LF_EINVAL, "prefill_paged: inconsistent shapes")
+    scale = D ** -0.5 if scale is None else float(scale)
+    o = torch.empty_like(q)
+    lse = torch.empty((T, Hq), dtype=torch.float32, device=q.device) if return_lse else None
+    _lib.call("lf_prefill_paged_fwd", q.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(),
+              block_table.data_ptr(), cu_seqlens_q.data_ptr(), seqlens_k.data_ptr(), o.data_ptr(),
+              lse.data_ptr() if lse is not None else None, N, T, int(max_seqlen_q), Hq, Hkv, D, P,
+              block_table.shape[1], scale, int(bool(causal)), _stream())
+    return (o, lse) if return_lse else o
+
+
 def default_pages_per_split(num_seqs: int, num_kv_heads: int, max_pages: int) -> int:
     """Split size: enough CTAs for several waves on 148 SMs, at most 128 pages each."""
     target_ctas = SM_COUNT * 3 * 8

@@ -36,6 +36,10 @@
 //   Dense  (prefill)  Q [B,Hq,Sq,D], K/V [B,Hkv,Sk,D]; an item = query tiles (2i, 2i+1) of one
 //                     (batch, head); causal mask with queries aligned to the end of the keys;
 //                     bf16 O normalised + natural-log LSE.
+//   Paged  (append)   varlen queries q [T_total, Hq, D] (session n owns rows cu_q[n]..cu_q[n+1])
+//                     over that session's pool pages (its block-table row, lk[n] tokens including
+//                     the new ones); an item = query tiles (2i, 2i+1) of one (session, query head);
+//                     causal mask with the queries at the end of the session; bf16 O + LSE.
 //   Prefix (decode)   an item = 2 x 128 query rows = 256/G sessions x G heads of one KV head and
 //                     one chunk of shared-prefix pages; q via 4-D TMA boxes over [N][Hkv][G][D];
 //                     K/V pages [P][Hkv][16][D] via 16-row boxes through the block table of the
@@ -74,7 +78,7 @@ constexpr float kRescaleThreshold = 8.0f;
 enum Bar { Q_FULL = 0, Q_EMPTY = 1, K_FULL = 2, K_EMPTY = 4, V_FULL = 6, V_EMPTY = 8, S_FULL = 10,
            P_FULL = 12, O_DONE = 14, NUM_BARS = 16 };
 
-enum class Mode { Dense, Prefix };
+enum class Mode { Dense, Paged, Prefix };
 
 struct Params {
     float c;
@@ -87,10 +91,13 @@ struct Params {
     float* part_o;
     float2* part_ml;
     int N, G, num_pages, max_pages, n_prefix, chunk_pages, n_chunks, n_qtiles, n_slots, slot0;
+    const int32_t* cu_q;     // paged: [N+1] query row offsets
+    int max_pairs;           // paged: tile pairs of the longest query run
 };
 
 struct Item {
-    int bhq, kvh, q_row0[2];                 // dense
+    int bhq, kvh, q_row0[2];                 // dense / paged
+    int sess, q_tok0, lq, lk;                // paged
     int h, n0, chunk, p_begin, p_end, src;   // prefix
     int nb[2];
     int nbk;
@@ -103,7 +110,29 @@ __device__ __forceinline__ Item item_coords(const Params& p, int w, int lane) {
     Item it;
     it.bhq = it.kvh = it.h = it.n0 = it.chunk = it.p_begin = it.p_end = it.src = 0;
     it.q_row0[0] = it.q_row0[1] = 0;
-    if constexpr (M == Mode::Dense) {
+    it.sess = it.q_tok0 = it.lq = it.lk = 0;
+    if constexpr (M == Mode::Paged) {
+        const int pair = p.max_pairs - 1 - w / (p.N * p.Hq);   // heavy pairs first
+        const int rest = w % (p.N * p.Hq);
+        it.sess = rest / p.Hq;
+        it.bhq = rest % p.Hq;                                   // query head
+        it.kvh = it.bhq / (p.Hq / p.Hkv);
+        it.q_tok0 = p.cu_q[it.sess];
+        it.lq = p.cu_q[it.sess + 1] - it.q_tok0;
+        it.lk = min(max(p.lens[it.sess], 0), p.max_pages * 16);
+        it.p_end = (it.lk + 15) / 16;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+            it.q_row0[t] = (2 * pair + t) * BM;
+            int n = 0;
+            if (it.q_row0[t] < it.lq) {
+                int kv_end = it.lk;
+                if (p.causal) kv_end = min(it.lk, it.q_row0[t] + BM + (it.lk - it.lq));
+                n = kv_end > 0 ? (kv_end + BN - 1) / BN : 0;
+            }
+            it.nb[t] = n;
+        }
+    } else if constexpr (M == Mode::Dense) {
         const int BH = p.B * p.Hq;
         it.bhq = w % BH;
         const int pair = p.n_pairs - 1 - w / BH;   // heavy pairs first
@@ -212,6 +241,10 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                         if constexpr (M == Mode::Dense) {
                             tma_load_3d(dst, &tmq, bar(Q_FULL), 0, it.q_row0[t], it.bhq);
                             tma_load_3d(dst + kHalfBytes, &tmq, bar(Q_FULL), 64, it.q_row0[t], it.bhq);
+                        } else if constexpr (M == Mode::Paged) {
+                            const int r0 = it.q_tok0 + it.q_row0[t];
+                            tma_load_3d(dst, &tmq, bar(Q_FULL), 0, it.bhq, r0);
+                            tma_load_3d(dst + kHalfBytes, &tmq, bar(Q_FULL), 64, it.bhq, r0);
                         } else {
                             const int nt = it.n0 + t * (BM / p.G);
                             tma_load_4d(dst, &tmq, bar(Q_FULL), 0, 0, it.h, nt);
@@ -221,6 +254,8 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                 }
                 const int32_t* bt_row = nullptr;
                 if constexpr (M == Mode::Prefix) bt_row = p.bt + (size_t)it.src * p.max_pages;
+                if constexpr (M == Mode::Paged) bt_row = p.bt + (size_t)it.sess * p.max_pages;
+                const int kv_head = (M == Mode::Paged) ? it.kvh : it.h;
                 auto load_kv = [&](const CUtensorMap* map, uint32_t dst, uint32_t full, int j) {
                     if constexpr (M == Mode::Dense) {
                         tma_load_3d(dst, map, full, 0, j * BN, it.kvh);
@@ -235,7 +270,7 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                                 if (static_cast<unsigned>(page) >= static_cast<unsigned>(p.num_pages))
                                     atomicCAS(&g_device_error, 0, 201);
                                 else
-                                    row = page * p.Hkv + it.h;
+                                    row = page * p.Hkv + kv_head;
                             }
                             tma_load_3d(dst + pg * kPageBoxBytes, map, full, 0, 0, row);
                             tma_load_3d(dst + kHalfBytes + pg * kPageBoxBytes, map, full, 64, 0, row);
@@ -366,6 +401,9 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
             if constexpr (M == Mode::Dense) {
                 qpos = it.q_row0[t] + row + p.q_offset;
                 key_limit = p.Sk;
+            } else if constexpr (M == Mode::Paged) {
+                qpos = it.q_row0[t] + row + (it.lk - it.lq);
+                key_limit = it.lk;
             } else {
                 const int rr = t * BM + row;
                 n = it.n0 + rr / p.G;
@@ -382,7 +420,7 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                 // in TMEM with -inf past lim, so the two passes below stay branch-free.
                 const int kbase = j * BN;
                 int lim = key_limit - kbase;
-                if constexpr (M == Mode::Dense)
+                if constexpr (M != Mode::Prefix)
                     if (p.causal) lim = min(lim, qpos - kbase + 1);
                 if (__any_sync(0xffffffffu, lim < BN)) {
 #pragma unroll 1
@@ -484,10 +522,14 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                 tc_fence_after();
             }
             // ---- epilogue: read O_t (the next item's first P.V may then overwrite it) ----
-            if constexpr (M == Mode::Dense) {
+            if constexpr (M != Mode::Prefix) {
+                // dense: o [B*Hq][Sq][D]; paged: o [T_total][Hq][D]; lse alike without D.
                 const int grow = it.q_row0[t] + row;
-                const size_t orow = static_cast<size_t>(it.bhq) * p.Sq + grow;
-                if (it.q_row0[t] < p.Sq) {
+                const int rows = (M == Mode::Dense) ? p.Sq : it.lq;
+                const size_t orow = (M == Mode::Dense)
+                                        ? static_cast<size_t>(it.bhq) * p.Sq + grow
+                                        : (static_cast<size_t>(it.q_tok0) + grow) * p.Hq + it.bhq;
+                if (it.q_row0[t] < rows) {
                     const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
 #pragma unroll 1
                     for (int cc = 0; cc < HD / 32; ++cc) {
@@ -499,7 +541,7 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
 #pragma unroll
                             for (int i = 0; i < 32; ++i) r[i] = 0u;
                         }
-                        if (grow < p.Sq) {
+                        if (grow < rows) {
                             uint4* dst = reinterpret_cast<uint4*>(p.o + orow * HD + cc * 32);
 #pragma unroll
                             for (int v = 0; v < 4; ++v) {
@@ -512,7 +554,7 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                             }
                         }
                     }
-                    if (p.lse != nullptr && grow < p.Sq)
+                    if (p.lse != nullptr && grow < rows)
                         p.lse[orow] = l_run > 0.f ? (m_run + log2f(l_run)) * kLn2 : -INFINITY;
                 }
             } else {

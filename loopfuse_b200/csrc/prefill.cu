@@ -70,6 +70,67 @@ extern "C" int lf_prefill_fwd(const lf_bf16* q, const lf_bf16* k, const lf_bf16*
     return launch_status("prefill");
 }
 
+extern "C" int lf_prefill_paged_fwd(const lf_bf16* q, const lf_bf16* k_pages,
+                                    const lf_bf16* v_pages, const int32_t* block_table,
+                                    const int32_t* cu_seqlens_q, const int32_t* seqlens_k,
+                                    lf_bf16* o, float* lse, int num_seqs, int total_q,
+                                    int max_seqlen_q, int num_q_heads, int num_kv_heads,
+                                    int head_dim, int num_pages, int max_pages, float scale,
+                                    int causal, void* stream) {
+    using namespace lf::tc2;
+    LF_CHECK_ARG(q && k_pages && v_pages && block_table && cu_seqlens_q && seqlens_k && o,
+                 "prefill paged: null pointer argument");
+    LF_CHECK_ARG(aligned16(q) && aligned16(k_pages) && aligned16(v_pages) && aligned16(o),
+                 "prefill paged: q, pages and o must be 16-byte aligned");
+    LF_CHECK_ARG(head_dim == HD, "prefill paged: head_dim must be %d (got %d)", HD, head_dim);
+    LF_CHECK_ARG(num_seqs > 0 && total_q > 0 && max_seqlen_q > 0 && num_kv_heads > 0 &&
+                     num_q_heads % num_kv_heads == 0 && num_pages > 0 && max_pages > 0,
+                 "prefill paged: bad sizes");
+    const long max_pairs = ((max_seqlen_q + BM - 1) / BM + 1) / 2;
+    const long n_items = max_pairs * num_seqs * num_q_heads;
+    LF_CHECK_ARG(n_items < 2147483647L, "prefill paged: too many work items");
+    CUtensorMap mq, mk, mv;
+    const cuuint64_t qdims[3] = {(cuuint64_t)HD, (cuuint64_t)num_q_heads, (cuuint64_t)total_q};
+    const cuuint64_t qstr[2] = {(cuuint64_t)HD * 2, (cuuint64_t)num_q_heads * HD * 2};
+    const cuuint32_t qbox[3] = {64, 1, 128};
+    const cuuint64_t pdims[3] = {(cuuint64_t)HD, 16, (cuuint64_t)num_pages * num_kv_heads};
+    const cuuint64_t pstr[2] = {(cuuint64_t)HD * 2, (cuuint64_t)16 * HD * 2};
+    const cuuint32_t pbox[3] = {64, 16, 1};
+    int rc = encode_bf16_map(&mq, q, 3, qdims, qstr, qbox);
+    if (rc) return rc;
+    rc = encode_bf16_map(&mk, k_pages, 3, pdims, pstr, pbox);
+    if (rc) return rc;
+    rc = encode_bf16_map(&mv, v_pages, 3, pdims, pstr, pbox);
+    if (rc) return rc;
+    static bool attr_set = false;
+    if (!attr_set) {
+        LF_CHECK_CUDA(cudaFuncSetAttribute(attn2_kernel<Mode::Paged>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+        attr_set = true;
+    }
+    Params p{};
+    p.c = scale * kLog2e;
+    p.o = o;
+    p.lse = lse;
+    p.Hq = num_q_heads;
+    p.Hkv = num_kv_heads;
+    p.causal = causal ? 1 : 0;
+    p.bt = block_table;
+    p.lens = seqlens_k;
+    p.cu_q = cu_seqlens_q;
+    p.N = num_seqs;
+    p.num_pages = num_pages;
+    p.max_pages = max_pages;
+    p.max_pairs = (int)max_pairs;
+    p.n_items = (int)n_items;
+    int sms = 0;
+    LF_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0));
+    const long grid = n_items < sms ? n_items : sms;
+    attn2_kernel<Mode::Paged><<<(unsigned)grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
+        mq, mk, mv, p);
+    return launch_status("prefill paged");
+}
+
 namespace lf {
 namespace decode {
 

@@ -248,6 +248,40 @@ class KVPool:
             s.current_len += n
         return start
 
+    def reserve(self, states: Sequence[KVState], counts: Sequence[int],
+                stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """Grow sessions by ``counts`` tokens (pages from the device queue); returns the device
+        tensor of their old lengths, the write offsets for ``write_layer``."""
+        return self._reserve(states, counts, stream)
+
+    def write_layer(self, states: Sequence[KVState], start: torch.Tensor, layer: int,
+                    keys: torch.Tensor, values: torch.Tensor, counts: Sequence[int],
+                    stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Store one layer's new K/V (``[T_total, Hkv, D]``, sessions back to back with
+        ``counts[i]`` tokens each) at the offsets a ``reserve`` returned.  A model forward
+        reserves once and then writes each layer as soon as its K/V exist."""
+        total = int(sum(counts))
+        if total == 0:
+            return
+        for t in (keys, values):
+            if t.device != self.device or t.dtype != self.dtype or not t.is_contiguous() or \
+                    tuple(t.shape) != (total, self.num_kv_heads, self.head_dim):
+                raise LoopfuseError(_lib.LF_EINVAL, "write_layer expects contiguous "
+                                                    "[T_total, Hkv, D] tensors of the pool dtype")
+        cu = [0]
+        for c in counts:
+            cu.append(cu[-1] + int(c))
+        ids = self._ids([s.slot_id for s in states])
+        cu_t = self._ids(cu)
+        elem = self.keys.element_size()
+        layer_off = layer * self.keys.stride(0) * elem
+        self._call("lf_pool_write_kv", self._meta_ref(), ids.data_ptr(), start.data_ptr(),
+                   cu_t.data_ptr(), len(states), total, keys.data_ptr(), values.data_ptr(), 0,
+                   keys.stride(0), keys.stride(1), self.keys.data_ptr() + layer_off,
+                   self.values.data_ptr() + layer_off, 1, self.num_kv_heads, self.head_dim,
+                   self._stream(stream))
+        self._bytes_written += 2 * keys.numel() * elem
+
     def append(self, states: Sequence[KVState], keys: Sequence[torch.Tensor],
                values: Sequence[torch.Tensor], layout: str = "lthd",
                stream: Optional[torch.cuda.Stream] = None) -> None:
