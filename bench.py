@@ -45,6 +45,9 @@ DECODE_WORKLOAD = ("paged decode: 256 sessions/GPU, 1 query token each, Hq=32 Hk
                    "16-token pages, L~U[1024,32768], 2048-token shared prefix, pool 1.1x demand, "
                    "random page permutation")
 PREFILL_WORKLOAD = "causal GQA prefill: B=8 Hq=32 Hkv=8 S=4096 D=128 bf16, scale 1/sqrt(128)"
+FUSION_WORKLOAD = ("KV-fusion loop: 64 sessions forked from a 4096-token prefix x 8 steps; per step "
+                   "a geometric(mean 120, cap 1024) tool-output append (paged prefill) and 64 "
+                   "decode tokens; 32 layers, Hq=32 Hkv=8 D=128 bf16 (attention and pool only)")
 
 
 def parse_args():
@@ -58,6 +61,7 @@ def parse_args():
     ap.add_argument("--sessions", type=int, default=256)
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-fusion", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=12, help="sessions in the CPU sample")
     return ap.parse_args()
 
@@ -323,11 +327,12 @@ def main():
     h2d = q_h.numel() * 2 + bt_h.numel() * 4 + ln_h.numel() * 4
     d2h = o_h.numel() * 2
 
+    del w, ws, out, q_h, bt_h, ln_h, o_h, q_d, bt_d, ln_d
+    torch.cuda.empty_cache()
+
     # ---------------- prefill op ----------------
     prefill = None
     if not args.no_prefill:
-        del w, ws, out, q_h, bt_h, ln_h, o_h, q_d, bt_d, ln_d
-        torch.cuda.empty_cache()
         B, PHq, PHkv, S = 8, 32, 8, 4096
         pq, pk, pv = prefill_inputs(B, PHq, PHkv, S, 128, seed=args.seed + 7 + 1000 * rank, device=dev)
         flops = prefill_flops(B, PHq, S, 128)
@@ -354,6 +359,29 @@ def main():
                                 "frac": round(tflops / peaks["bf16_tflops"], 4),
                                 "traffic": profile_traffic("prefill_causal_b8_s4096.txt"),
                                 "peak_source": peaks["source"] + " (burst)"}}
+
+    # ---------------- KV-fusion loop (64 sessions x 8 steps, Llama-3-8B attention shapes) ----
+    fusion = None
+    if not args.no_fusion:
+        torch.cuda.empty_cache()
+        from loopfuse_b200.kv_fusion_loop import FusionLoop, FusionLoopConfig
+        loop = FusionLoop(FusionLoopConfig(seed=args.seed + rank), device=dev)
+        barrier()
+        res = loop.run()
+        steps_ = res.steps
+        f_ms = max_over_ranks(sum(s.ms for s in steps_))
+        rd = sum(s.bytes_read for s in steps_)
+        fusion = {"workload": FUSION_WORKLOAD, "ms_total": round(f_ms, 2),
+                  "ms_per_step": round(f_ms / len(steps_), 2),
+                  "hbm_bytes_read_per_step": [s.bytes_read for s in steps_],
+                  "hbm_bytes_read_per_step_unshared": [s.bytes_read_unshared for s in steps_],
+                  "hbm_bytes_written_per_step": [s.bytes_written for s in steps_],
+                  "tool_tokens_per_step": [s.tool_tokens for s in steps_],
+                  "read_GBps": round(world * rd / (f_ms * 1e-3) / 1e9, 1),
+                  "sharing_saves_frac": round(1 - rd / sum(s.bytes_read_unshared for s in steps_), 4),
+                  "gpu_launches": sum(s.launches for s in steps_)}
+        del loop
+        torch.cuda.empty_cache()
 
     # ---------------- CPU baseline (rank 0, N=1) ----------------
     cpu = None
@@ -393,6 +421,7 @@ def main():
             "gpu_launches": launches_per_step * K,
             "clocks": clocks,
             "prefill": prefill,
+            "kv_fusion_loop": fusion,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

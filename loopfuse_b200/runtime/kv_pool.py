@@ -254,13 +254,21 @@ class KVPool:
         tensor of their old lengths, the write offsets for ``write_layer``."""
         return self._reserve(states, counts, stream)
 
+    def batch_index(self, states: Sequence[KVState], counts: Sequence[int]
+                    ) -> Tuple[torch.Tensor, torch.Tensor, int]:
+        """Device (session ids, token offsets, total) of a batch, reusable across layers."""
+        cu = [0]
+        for c in counts:
+            cu.append(cu[-1] + int(c))
+        return self._ids([s.slot_id for s in states]), self._ids(cu), cu[-1]
+
     def write_layer(self, states: Sequence[KVState], start: torch.Tensor, layer: int,
                     keys: torch.Tensor, values: torch.Tensor, counts: Sequence[int],
-                    stream: Optional[torch.cuda.Stream] = None) -> None:
+                    stream: Optional[torch.cuda.Stream] = None, index=None) -> None:
         """Store one layer's new K/V (``[T_total, Hkv, D]``, sessions back to back with
         ``counts[i]`` tokens each) at the offsets a ``reserve`` returned.  A model forward
         reserves once and then writes each layer as soon as its K/V exist."""
-        total = int(sum(counts))
+        ids, cu_t, total = index if index is not None else self.batch_index(states, counts)
         if total == 0:
             return
         for t in (keys, values):
@@ -268,11 +276,6 @@ class KVPool:
                     tuple(t.shape) != (total, self.num_kv_heads, self.head_dim):
                 raise LoopfuseError(_lib.LF_EINVAL, "write_layer expects contiguous "
                                                     "[T_total, Hkv, D] tensors of the pool dtype")
-        cu = [0]
-        for c in counts:
-            cu.append(cu[-1] + int(c))
-        ids = self._ids([s.slot_id for s in states])
-        cu_t = self._ids(cu)
         elem = self.keys.element_size()
         layer_off = layer * self.keys.stride(0) * elem
         self._call("lf_pool_write_kv", self._meta_ref(), ids.data_ptr(), start.data_ptr(),
