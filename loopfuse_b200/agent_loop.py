@@ -1,0 +1,202 @@
+"""Many concurrent ReAct agent sessions on one GPU: batched prefill / decode with tool waits.
+
+This is the runtime side of the reference's agent programs (``runtime/executor.py`` runs one
+program's steps sequentially; ``passes/spec_prefill.py:59-124`` inserts speculative prefills
+before tool calls).  Every session runs ``steps`` ReAct steps: the observation tokens (the
+user question on the first step, the previous tool's output after that) are prefilled, the
+model decodes ``decode_tokens`` tokens (thought + action), then the tool runs on the host for an
+exponentially distributed latency (mean ``tool_ms``) while the GPU serves other sessions.
+
+Scheduling (one host thread per GPU, a loop of GPU batches):
+  1. sessions whose tool has returned move to "prefill";
+  2. if any session waits for prefill, one varlen prefill batch of all of them (capped at
+     ``max_prefill_tokens``) runs and yields each session's first decoded token;
+  3. otherwise one decode iteration advances every decoding session by one token; sessions
+     that finish their thought/action start their tool call;
+  4. if nothing is runnable, the GPU would idle until the next tool returns: speculative
+     prefill fills that window.  Every observation begins with the same template tokens
+     ("Observation:"), so while a session's tool runs, those ``spec_tokens`` tokens are
+     prefilled ahead of time (on the pool's low-priority stream); when the tool returns only
+     the tool output itself is left to prefill.
+The system prompt (``prefix_tokens``) is prefilled once and forked to every session, so the
+decode attention reads it once per group of sessions.
+
+Token ids are synthetic (seeded uniform ids; tool outputs of geometric length, mean
+``tool_len_mean``, capped).  The reported metric is agent steps per second: completed ReAct
+steps of all sessions divided by the wall time of the loop.
+"""
+from __future__ import annotations
+
+import heapq
+import time
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional
+
+import numpy as np
+import torch
+
+from .llama import LlamaShaped
+from .runtime.kv_pool import KVPool, KVState
+
+PAGE = 16
+
+
+@dataclass
+class AgentLoopConfig:
+    sessions: int = 512
+    steps: int = 10
+    prefix_tokens: int = 4096
+    question_tokens: int = 128
+    decode_tokens: int = 32
+    tool_ms: float = 100.0
+    tool_len_mean: float = 120.0
+    tool_len_cap: int = 1024
+    spec_tokens: int = 4
+    speculative: bool = True
+    max_prefill_tokens: int = 16384
+    seed: int = 0
+
+
+@dataclass
+class _Sess:
+    idx: int
+    state: KVState
+    pos: int = 0
+    step: int = 0
+    phase: str = "prefill"          # prefill | decode | tool | done
+    pending: List[int] = field(default_factory=list)
+    decoded: int = 0
+    last_token: int = 0
+    spec_done: bool = False
+    ready_at: float = 0.0
+
+
+@dataclass
+class AgentLoopStats:
+    sessions: int = 0
+    steps_done: int = 0
+    wall_s: float = 0.0
+    steps_per_s: float = 0.0
+    prefill_batches: int = 0
+    decode_iters: int = 0
+    spec_batches: int = 0
+    spec_tokens: int = 0
+    prefill_tokens: int = 0
+    decode_tokens: int = 0
+    gpu_busy_s: float = 0.0
+    idle_waits: int = 0
+
+
+class AgentLoop:
+    def __init__(self, model: LlamaShaped, cfg: AgentLoopConfig, session_ids: Optional[List[int]] = None,
+                 device=None):
+        self.model, self.cfg = model, cfg
+        self.device = torch.device(device or model.device)
+        self.ids = list(range(cfg.sessions)) if session_ids is None else list(session_ids)
+        rng = np.random.default_rng(cfg.seed)
+        # per (global session id, step) tool-output lengths and latencies: the same on every rank
+        self.tool_len = np.minimum(rng.geometric(1.0 / cfg.tool_len_mean,
+                                                 size=(cfg.sessions, cfg.steps)), cfg.tool_len_cap)
+        self.tool_lat = rng.exponential(cfg.tool_ms / 1000.0, size=(cfg.sessions, cfg.steps))
+        self.vocab = model.cfg.vocab
+        self.template = [int(x) for x in rng.integers(0, self.vocab, size=cfg.spec_tokens)]
+        n = len(self.ids)
+        own = [cfg.question_tokens + int(self.tool_len[i].sum()) +
+               cfg.steps * (cfg.decode_tokens + cfg.spec_tokens) for i in self.ids]
+        max_len = cfg.prefix_tokens + max(own) + 64
+        self.n_prefix_pages = cfg.prefix_tokens // PAGE
+        pages = self.n_prefix_pages + sum((o + PAGE - 1) // PAGE + 1 for o in own) + 16
+        mc = model.cfg
+        self.pool = KVPool(num_layers=mc.layers, num_heads=mc.q_heads, num_kv_heads=mc.kv_heads,
+                           head_dim=mc.head_dim, max_seq_len=max_len, max_slots=n + 1,
+                           dtype=torch.bfloat16, device=self.device, num_pages=pages)
+        self.rng = np.random.default_rng(cfg.seed + 17)
+
+    def _ids_tensor(self, toks: List[int]) -> torch.Tensor:
+        return torch.tensor(toks, dtype=torch.long).to(self.device, non_blocking=True)
+
+    def _run(self, sess: List[_Sess], chunks: List[List[int]], stats: AgentLoopStats) -> List[int]:
+        toks = [t for ch in chunks for t in ch]
+        t0 = time.perf_counter()
+        nxt = self.model.forward(self._ids_tensor(toks), self.pool, [s.state for s in sess],
+                                 [len(ch) for ch in chunks], n_prefix_pages=self.n_prefix_pages)
+        out = nxt.tolist()                          # one host sync per batch
+        stats.gpu_busy_s += time.perf_counter() - t0
+        return out
+
+    def run(self) -> AgentLoopStats:
+        cfg, pool = self.cfg, self.pool
+        stats = AgentLoopStats(sessions=len(self.ids))
+        t_start = time.perf_counter()
+        # shared system prompt, prefilled once, forked to every session
+        root = pool.alloc()
+        sys_prompt = [int(x) for x in self.rng.integers(0, self.vocab, size=cfg.prefix_tokens)]
+        self._run([_Sess(-1, root)], [sys_prompt], stats)
+        states = pool.fork(root, cfg.prefix_tokens, n=len(self.ids))
+        sessions = [_Sess(i, st, k) for k, (i, st) in enumerate(zip(self.ids, states))]
+        for s in sessions:
+            s.pending = [int(x) for x in self.rng.integers(0, self.vocab, size=cfg.question_tokens)]
+        tools: List = []                            # heap of (ready_at, idx in sessions)
+        while True:
+            now = time.perf_counter()
+            while tools and tools[0][0] <= now:
+                _, k = heapq.heappop(tools)
+                s = sessions[k]
+                out_len = int(self.tool_len[s.idx, s.step - 1])
+                obs = [] if s.spec_done else list(self.template)
+                s.pending = obs + [int(x) for x in self.rng.integers(0, self.vocab, size=out_len)]
+                s.phase = "prefill"
+            pre = [s for s in sessions if s.phase == "prefill"]
+            dec = [s for s in sessions if s.phase == "decode"]
+            if pre:
+                batch, budget = [], cfg.max_prefill_tokens
+                for s in pre:
+                    if batch and len(s.pending) > budget:
+                        break
+                    batch.append(s)
+                    budget -= len(s.pending)
+                nxt = self._run(batch, [s.pending for s in batch], stats)
+                stats.prefill_batches += 1
+                stats.prefill_tokens += sum(len(s.pending) for s in batch)
+                for s, t in zip(batch, nxt):
+                    s.pending, s.last_token, s.decoded, s.phase = [], t, 1, "decode"
+                    s.spec_done = False
+                continue
+            if dec:
+                nxt = self._run(dec, [[s.last_token] for s in dec], stats)
+                stats.decode_iters += 1
+                stats.decode_tokens += len(dec)
+                now = time.perf_counter()
+                for s, t in zip(dec, nxt):
+                    s.last_token = t
+                    s.decoded += 1
+                    if s.decoded >= cfg.decode_tokens:
+                        s.step += 1
+                        stats.steps_done += 1
+                        if s.step >= cfg.steps:
+                            s.phase = "done"
+                        else:
+                            s.phase = "tool"
+                            s.ready_at = now + float(self.tool_lat[s.idx, s.step - 1])
+                            heapq.heappush(tools, (s.ready_at, s.pos))
+                continue
+            if not tools:
+                break
+            # idle window: speculative prefill of the observation template
+            spec = [s for s in sessions if s.phase == "tool" and not s.spec_done] if cfg.speculative else []
+            if spec:
+                with torch.cuda.stream(pool.prefetch_stream):
+                    self._run(spec, [list(self.template) for _ in spec], stats)
+                torch.cuda.current_stream().wait_stream(pool.prefetch_stream)
+                for s in spec:
+                    s.spec_done = True
+                stats.spec_batches += 1
+                stats.spec_tokens += len(spec) * cfg.spec_tokens
+                continue
+            stats.idle_waits += 1
+            time.sleep(max(0.0, min(tools[0][0] - time.perf_counter(), 0.002)))
+        torch.cuda.synchronize(self.device)
+        stats.wall_s = time.perf_counter() - t_start
+        stats.steps_per_s = stats.steps_done / stats.wall_s
+        pool.release_all(states + [root])
+        return stats

@@ -1,0 +1,75 @@
+"""The Llama-shaped model and the agent loop on small configurations.
+
+Model parity: our forward (bf16 activations, cuBLAS GEMMs, sm_100a paged prefill / decode,
+pool appends) against an fp32 torch restatement with the same weights and the CPU attention
+oracle, for a prefill followed by teacher-forced decode steps.
+"""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import attention as ora
+from loopfuse_b200.agent_loop import AgentLoop, AgentLoopConfig
+from loopfuse_b200.llama import LlamaConfig, LlamaShaped
+from loopfuse_b200.runtime.kv_pool import KVPool
+
+pytestmark = pytest.mark.gpu
+
+SMALL = LlamaConfig(d_model=256, layers=2, q_heads=4, kv_heads=2, head_dim=128, ffn=512, vocab=1000)
+
+
+def _reference_logits(m: LlamaShaped, tokens: torch.Tensor) -> torch.Tensor:
+    """fp32 restatement over the whole sequence; logits of the last position."""
+    c = m.cfg
+    T = tokens.numel()
+    x = m.embed[tokens].float().cpu()
+    pos = torch.arange(T).float()
+    ang = pos[:, None] * m.inv_freq.cpu()[None, :]
+    cos, sin = ang.cos()[:, None, :], ang.sin()[:, None, :]
+
+    def rms(v, w):
+        return v * torch.rsqrt(v.pow(2).mean(-1, keepdim=True) + c.eps) * w.float().cpu()
+
+    def rope(v):
+        h = v.shape[-1] // 2
+        return torch.cat([v[..., :h] * cos - v[..., h:] * sin, v[..., h:] * cos + v[..., :h] * sin], -1)
+
+    nq, nk = c.q_heads * c.head_dim, c.kv_heads * c.head_dim
+    for l in range(c.layers):
+        h = rms(x, m.attn_norm[l])
+        qkv = h @ m.wqkv[l].float().cpu()
+        q = rope(qkv[:, :nq].view(T, c.q_heads, c.head_dim))
+        k = rope(qkv[:, nq:nq + nk].view(T, c.kv_heads, c.head_dim))
+        v = qkv[:, nq + nk:].view(T, c.kv_heads, c.head_dim)
+        o, _ = ora.prefill(q.permute(1, 0, 2)[None], k.permute(1, 0, 2)[None], v.permute(1, 0, 2)[None])
+        x = x + o[0].permute(1, 0, 2).reshape(T, nq) @ m.wo[l].float().cpu()
+        h = rms(x, m.ffn_norm[l])
+        gu = h @ m.w13[l].float().cpu()
+        x = x + (F.silu(gu[:, :c.ffn]) * gu[:, c.ffn:]) @ m.w2[l].float().cpu()
+    return (rms(x[-1:], m.final_norm) @ m.lm_head.float().cpu())[0]
+
+
+def test_model_prefill_then_decode_matches_fp32_reference():
+    m = LlamaShaped(SMALL, seed=1, std=0.05)
+    pool = KVPool(num_layers=SMALL.layers, num_heads=SMALL.q_heads, num_kv_heads=SMALL.kv_heads,
+                  head_dim=SMALL.head_dim, max_seq_len=256, max_slots=2, dtype=torch.bfloat16)
+    s = pool.allocate_slot()
+    g = torch.Generator().manual_seed(0)
+    toks = torch.randint(0, SMALL.vocab, (43,), generator=g)
+    got = m.forward(toks[:40].cuda(), pool, [s], [40], return_logits=True)[0].cpu()
+    for i in range(40, 43):                                   # teacher-forced decode
+        ref = _reference_logits(m, toks[:i])
+        cos = F.cosine_similarity(got, ref, dim=0).item()
+        assert cos > 0.999, (i, cos)
+        assert (got - ref).abs().max().item() < 0.1 * ref.abs().max().item()
+        got = m.forward(toks[i:i + 1].cuda(), pool, [s], [1], return_logits=True)[0].cpu()
+
+
+def test_small_agent_loop_completes_every_step():
+    m = LlamaShaped(SMALL, seed=2)
+    cfg = AgentLoopConfig(sessions=6, steps=2, prefix_tokens=64, question_tokens=16, decode_tokens=3,
+                          tool_ms=5.0, tool_len_mean=10, tool_len_cap=20, spec_tokens=4, seed=3)
+    st = AgentLoop(m, cfg).run()
+    assert st.steps_done == cfg.sessions * cfg.steps
+    assert st.decode_tokens >= cfg.sessions * cfg.steps * (cfg.decode_tokens - 1)
+    assert st.steps_per_s > 0
