@@ -65,8 +65,8 @@ int lf_device_status(int* out);
  * o [B,Hq,Sq,D]; query head h reads KV head h / (Hq/Hkv).  causal != 0 masks
  * key j for query i when j > i + (Sk - Sq) (the reference's q >= k mask when
  * Sq == Sk, prefill_attn.py:97-99).  lse [B,Hq,Sq] (nullable) receives the
- * natural-log log-sum-exp of each row.  D must be 128; all pointers 16-byte
- * aligned.  tcgen05 MMA with TMEM accumulators, TMA-loaded tiles. */
+ * natural-log log-sum-exp of each row.  D must be 128 or 64; all pointers
+ * 16-byte aligned.  tcgen05 MMA with TMEM accumulators, TMA-loaded tiles. */
 int lf_prefill_fwd(const lf_bf16* q, const lf_bf16* k, const lf_bf16* v, lf_bf16* o,
                    float* lse, int batch, int num_q_heads, int num_kv_heads, int seq_q,
                    int seq_k, int head_dim, float scale, int causal, void* stream);

@@ -42,7 +42,7 @@ def _require(t: torch.Tensor, name: str, dtype=torch.bfloat16) -> None:
 
 def prefill_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
                           scale: Optional[float] = None, return_lse: bool = False):
-    """Causal GQA attention: ``q [B,Hq,Sq,D]``, ``k, v [B,Hkv,Sk,D]`` -> ``o [B,Hq,Sq,D]``."""
+    """Causal GQA attention: ``q [B,Hq,Sq,D]``, ``k, v [B,Hkv,Sk,D]`` -> ``o [B,Hq,Sq,D]``, D 64 or 128."""
     for t, n in ((q, "q"), (k, "k"), (v, "v")):
         _require(t, n)
     B, Hq, Sq, D = q.shape

@@ -62,9 +62,9 @@ using namespace sm100;
 
 constexpr int BM = 128;
 constexpr int BN = 128;
-constexpr int HD = 128;
+constexpr int kMaxHD = 128;                       // buffers are sized for head_dim 128
 constexpr int kThreads = 384;
-constexpr uint32_t kTileBytes = BM * HD * 2;      // 32 KB
+constexpr uint32_t kTileBytes = BM * kMaxHD * 2;  // 32 KB
 constexpr uint32_t kHalfBytes = kTileBytes / 2;   // 16 KB: [128 rows][64 dims]
 constexpr uint32_t kPageBoxBytes = 16 * 64 * 2;   // 2 KB: [16 rows][64 dims]
 constexpr uint32_t OFF_Q = 0;                            // 2 tiles
@@ -181,10 +181,15 @@ __device__ __forceinline__ Item item_coords(const Params& p, int w, int lane) {
     return it;
 }
 
-template <Mode M>
+// HDIM: head_dim, 128 or 64.  At 64 a tile is a single 128-byte-swizzled [rows][64] box and the
+// MMAs run with K = 64 (QK^T) and N = 64 (P.V).
+template <Mode M, int HDIM>
 __global__ void __launch_bounds__(kThreads, 1)
 attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
              const __grid_constant__ CUtensorMap tmv, const Params p) {
+    static_assert(HDIM == 128 || HDIM == 64, "head_dim must be 64 or 128");
+    constexpr int HD = HDIM;
+    constexpr uint32_t kLoadBytes = BM * HD * 2;      // bytes of one Q, K or V tile
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
@@ -234,21 +239,21 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
             if (lane == 0) {
                 if (qi > 0) ok = mbar_wait(bar(Q_EMPTY), (qi - 1) & 1, abort_flag, 12);
                 if (ok) {
-                    mbar_arrive_expect_tx(bar(Q_FULL), 2 * kTileBytes);
+                    mbar_arrive_expect_tx(bar(Q_FULL), 2 * kLoadBytes);
 #pragma unroll
                     for (int t = 0; t < 2; ++t) {
-                        const uint32_t dst = sbase + OFF_Q + t * kTileBytes;
-                        if constexpr (M == Mode::Dense) {
-                            tma_load_3d(dst, &tmq, bar(Q_FULL), 0, it.q_row0[t], it.bhq);
-                            tma_load_3d(dst + kHalfBytes, &tmq, bar(Q_FULL), 64, it.q_row0[t], it.bhq);
-                        } else if constexpr (M == Mode::Paged) {
-                            const int r0 = it.q_tok0 + it.q_row0[t];
-                            tma_load_3d(dst, &tmq, bar(Q_FULL), 0, it.bhq, r0);
-                            tma_load_3d(dst + kHalfBytes, &tmq, bar(Q_FULL), 64, it.bhq, r0);
-                        } else {
-                            const int nt = it.n0 + t * (BM / p.G);
-                            tma_load_4d(dst, &tmq, bar(Q_FULL), 0, 0, it.h, nt);
-                            tma_load_4d(dst + kHalfBytes, &tmq, bar(Q_FULL), 64, 0, it.h, nt);
+#pragma unroll
+                        for (int hf = 0; hf < HD / 64; ++hf) {
+                            const uint32_t dst = sbase + OFF_Q + t * kTileBytes + hf * kHalfBytes;
+                            if constexpr (M == Mode::Dense) {
+                                tma_load_3d(dst, &tmq, bar(Q_FULL), hf * 64, it.q_row0[t], it.bhq);
+                            } else if constexpr (M == Mode::Paged) {
+                                tma_load_3d(dst, &tmq, bar(Q_FULL), hf * 64, it.bhq,
+                                            it.q_tok0 + it.q_row0[t]);
+                            } else {
+                                tma_load_4d(dst, &tmq, bar(Q_FULL), hf * 64, 0, it.h,
+                                            it.n0 + t * (BM / p.G));
+                            }
                         }
                     }
                 }
@@ -258,8 +263,9 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                 const int kv_head = (M == Mode::Paged) ? it.kvh : it.h;
                 auto load_kv = [&](const CUtensorMap* map, uint32_t dst, uint32_t full, int j) {
                     if constexpr (M == Mode::Dense) {
-                        tma_load_3d(dst, map, full, 0, j * BN, it.kvh);
-                        tma_load_3d(dst + kHalfBytes, map, full, 64, j * BN, it.kvh);
+#pragma unroll
+                        for (int hf = 0; hf < HD / 64; ++hf)
+                            tma_load_3d(dst + hf * kHalfBytes, map, full, hf * 64, j * BN, it.kvh);
                     } else {
 #pragma unroll 1
                         for (int pg = 0; pg < 8; ++pg) {
@@ -272,8 +278,10 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                                 else
                                     row = page * p.Hkv + kv_head;
                             }
-                            tma_load_3d(dst + pg * kPageBoxBytes, map, full, 0, 0, row);
-                            tma_load_3d(dst + kHalfBytes + pg * kPageBoxBytes, map, full, 64, 0, row);
+#pragma unroll
+                            for (int hf = 0; hf < HD / 64; ++hf)
+                                tma_load_3d(dst + hf * kHalfBytes + pg * kPageBoxBytes, map, full,
+                                            hf * 64, 0, row);
                         }
                     }
                 };
@@ -281,10 +289,10 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                     const int gj = g + j, st = gj & 1;
                     const uint32_t ph = (gj >> 1) & 1;
                     if (!(ok = mbar_wait(bar(K_EMPTY + st), ph ^ 1, abort_flag, 1))) break;
-                    mbar_arrive_expect_tx(bar(K_FULL + st), kTileBytes);
+                    mbar_arrive_expect_tx(bar(K_FULL + st), kLoadBytes);
                     load_kv(&tmk, sbase + OFF_K + st * kTileBytes, bar(K_FULL + st), j);
                     if (!(ok = mbar_wait(bar(V_EMPTY + st), ph ^ 1, abort_flag, 2))) break;
-                    mbar_arrive_expect_tx(bar(V_FULL + st), kTileBytes);
+                    mbar_arrive_expect_tx(bar(V_FULL + st), kLoadBytes);
                     load_kv(&tmv, sbase + OFF_V + st * kTileBytes, bar(V_FULL + st), j);
                 }
             }

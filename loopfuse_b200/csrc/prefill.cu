@@ -12,6 +12,83 @@
 
 using namespace lf;
 
+namespace {
+
+template <lf::tc2::Mode M, int HD>
+int set_smem_attr() {
+    static bool done = false;
+    if (!done) {
+        LF_CHECK_CUDA(cudaFuncSetAttribute(lf::tc2::attn2_kernel<M, HD>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)lf::tc2::kSmemBytes));
+        done = true;
+    }
+    return LF_OK;
+}
+
+int sm_count(int* sms) {
+    int dev = 0;
+    LF_CHECK_CUDA(cudaGetDevice(&dev));
+    LF_CHECK_CUDA(cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, dev));
+    return LF_OK;
+}
+
+template <int HD>
+int launch_dense(const lf_bf16* q, const lf_bf16* k, const lf_bf16* v, lf::tc2::Params p,
+                 long n_items, cudaStream_t st) {
+    using namespace lf::tc2;
+    // [B*H][S][HD] bf16 views; [128 rows][64 dims] boxes.
+    CUtensorMap mq, mk, mv;
+    const cuuint32_t box[3] = {64, 128, 1};
+    const cuuint64_t qdims[3] = {(cuuint64_t)HD, (cuuint64_t)p.Sq, (cuuint64_t)p.B * p.Hq};
+    const cuuint64_t qstr[2] = {(cuuint64_t)HD * 2, (cuuint64_t)p.Sq * HD * 2};
+    const cuuint64_t kdims[3] = {(cuuint64_t)HD, (cuuint64_t)p.Sk, (cuuint64_t)p.B * p.Hkv};
+    const cuuint64_t kstr[2] = {(cuuint64_t)HD * 2, (cuuint64_t)p.Sk * HD * 2};
+    int rc = lf::encode_bf16_map(&mq, q, 3, qdims, qstr, box);
+    if (rc) return rc;
+    rc = lf::encode_bf16_map(&mk, k, 3, kdims, kstr, box);
+    if (rc) return rc;
+    rc = lf::encode_bf16_map(&mv, v, 3, kdims, kstr, box);
+    if (rc) return rc;
+    rc = set_smem_attr<Mode::Dense, HD>();
+    if (rc) return rc;
+    int sms = 0;
+    rc = sm_count(&sms);
+    if (rc) return rc;
+    const long grid = n_items < sms ? n_items : sms;   // persistent: one CTA per SM
+    attn2_kernel<Mode::Dense, HD><<<(unsigned)grid, kThreads, kSmemBytes, st>>>(mq, mk, mv, p);
+    return lf::launch_status("prefill");
+}
+
+template <int HD>
+int launch_paged(const lf_bf16* q, const lf_bf16* kp, const lf_bf16* vp, int total_q, lf::tc2::Params p,
+                 long n_items, cudaStream_t st) {
+    using namespace lf::tc2;
+    CUtensorMap mq, mk, mv;
+    const cuuint64_t qdims[3] = {(cuuint64_t)HD, (cuuint64_t)p.Hq, (cuuint64_t)total_q};
+    const cuuint64_t qstr[2] = {(cuuint64_t)HD * 2, (cuuint64_t)p.Hq * HD * 2};
+    const cuuint32_t qbox[3] = {64, 1, 128};
+    const cuuint64_t pdims[3] = {(cuuint64_t)HD, 16, (cuuint64_t)p.num_pages * p.Hkv};
+    const cuuint64_t pstr[2] = {(cuuint64_t)HD * 2, (cuuint64_t)16 * HD * 2};
+    const cuuint32_t pbox[3] = {64, 16, 1};
+    int rc = lf::encode_bf16_map(&mq, q, 3, qdims, qstr, qbox);
+    if (rc) return rc;
+    rc = lf::encode_bf16_map(&mk, kp, 3, pdims, pstr, pbox);
+    if (rc) return rc;
+    rc = lf::encode_bf16_map(&mv, vp, 3, pdims, pstr, pbox);
+    if (rc) return rc;
+    rc = set_smem_attr<Mode::Paged, HD>();
+    if (rc) return rc;
+    int sms = 0;
+    rc = sm_count(&sms);
+    if (rc) return rc;
+    const long grid = n_items < sms ? n_items : sms;
+    attn2_kernel<Mode::Paged, HD><<<(unsigned)grid, kThreads, kSmemBytes, st>>>(mq, mk, mv, p);
+    return lf::launch_status("prefill paged");
+}
+
+}  // namespace
+
 extern "C" int lf_prefill_fwd(const lf_bf16* q, const lf_bf16* k, const lf_bf16* v, lf_bf16* o,
                               float* lse, int batch, int num_q_heads, int num_kv_heads, int seq_q,
                               int seq_k, int head_dim, float scale, int causal, void* stream) {
@@ -19,7 +96,8 @@ extern "C" int lf_prefill_fwd(const lf_bf16* q, const lf_bf16* k, const lf_bf16*
     LF_CHECK_ARG(q && k && v && o, "prefill: null pointer argument");
     LF_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o),
                  "prefill: q, k, v, o must be 16-byte aligned");
-    LF_CHECK_ARG(head_dim == HD, "prefill: head_dim must be %d (got %d)", HD, head_dim);
+    LF_CHECK_ARG(head_dim == 128 || head_dim == 64, "prefill: head_dim must be 64 or 128 (got %d)",
+                 head_dim);
     LF_CHECK_ARG(batch > 0 && num_q_heads > 0 && num_kv_heads > 0 && num_q_heads % num_kv_heads == 0,
                  "prefill: need Hq a positive multiple of Hkv");
     LF_CHECK_ARG(seq_q > 0 && seq_k > 0, "prefill: sequence lengths must be positive");
@@ -27,30 +105,6 @@ extern "C" int lf_prefill_fwd(const lf_bf16* q, const lf_bf16* k, const lf_bf16*
     const long n_pairs = (n_qt + 1) / 2;
     const long n_items = n_pairs * batch * num_q_heads;
     LF_CHECK_ARG(n_items < 2147483647L, "prefill: too many query tiles");
-    int sms = 0;
-    LF_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0));
-    const long grid = n_items < sms ? n_items : sms;   // persistent: one CTA per SM
-
-    // [B*H][S][128] bf16 views; [128 rows][64 dims] boxes.
-    CUtensorMap mq, mk, mv;
-    const cuuint32_t box[3] = {64, 128, 1};
-    const cuuint64_t qdims[3] = {(cuuint64_t)HD, (cuuint64_t)seq_q, (cuuint64_t)batch * num_q_heads};
-    const cuuint64_t qstr[2] = {(cuuint64_t)HD * 2, (cuuint64_t)seq_q * HD * 2};
-    const cuuint64_t kdims[3] = {(cuuint64_t)HD, (cuuint64_t)seq_k, (cuuint64_t)batch * num_kv_heads};
-    const cuuint64_t kstr[2] = {(cuuint64_t)HD * 2, (cuuint64_t)seq_k * HD * 2};
-    int rc = encode_bf16_map(&mq, q, 3, qdims, qstr, box);
-    if (rc) return rc;
-    rc = encode_bf16_map(&mk, k, 3, kdims, kstr, box);
-    if (rc) return rc;
-    rc = encode_bf16_map(&mv, v, 3, kdims, kstr, box);
-    if (rc) return rc;
-
-    static bool attr_set = false;
-    if (!attr_set) {
-        LF_CHECK_CUDA(cudaFuncSetAttribute(attn2_kernel<Mode::Dense>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
-        attr_set = true;
-    }
     Params p{};
     p.c = scale * kLog2e;
     p.o = o;
@@ -65,9 +119,9 @@ extern "C" int lf_prefill_fwd(const lf_bf16* q, const lf_bf16* k, const lf_bf16*
     p.n_items = (int)n_items;
     p.causal = causal ? 1 : 0;
     p.q_offset = seq_k - seq_q;
-    attn2_kernel<Mode::Dense><<<(unsigned)grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
-        mq, mk, mv, p);
-    return launch_status("prefill");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    return head_dim == 128 ? launch_dense<128>(q, k, v, p, n_items, st)
+                           : launch_dense<64>(q, k, v, p, n_items, st);
 }
 
 extern "C" int lf_prefill_paged_fwd(const lf_bf16* q, const lf_bf16* k_pages,
@@ -82,32 +136,14 @@ extern "C" int lf_prefill_paged_fwd(const lf_bf16* q, const lf_bf16* k_pages,
                  "prefill paged: null pointer argument");
     LF_CHECK_ARG(aligned16(q) && aligned16(k_pages) && aligned16(v_pages) && aligned16(o),
                  "prefill paged: q, pages and o must be 16-byte aligned");
-    LF_CHECK_ARG(head_dim == HD, "prefill paged: head_dim must be %d (got %d)", HD, head_dim);
+    LF_CHECK_ARG(head_dim == 128 || head_dim == 64,
+                 "prefill paged: head_dim must be 64 or 128 (got %d)", head_dim);
     LF_CHECK_ARG(num_seqs > 0 && total_q > 0 && max_seqlen_q > 0 && num_kv_heads > 0 &&
                      num_q_heads % num_kv_heads == 0 && num_pages > 0 && max_pages > 0,
                  "prefill paged: bad sizes");
     const long max_pairs = ((max_seqlen_q + BM - 1) / BM + 1) / 2;
     const long n_items = max_pairs * num_seqs * num_q_heads;
     LF_CHECK_ARG(n_items < 2147483647L, "prefill paged: too many work items");
-    CUtensorMap mq, mk, mv;
-    const cuuint64_t qdims[3] = {(cuuint64_t)HD, (cuuint64_t)num_q_heads, (cuuint64_t)total_q};
-    const cuuint64_t qstr[2] = {(cuuint64_t)HD * 2, (cuuint64_t)num_q_heads * HD * 2};
-    const cuuint32_t qbox[3] = {64, 1, 128};
-    const cuuint64_t pdims[3] = {(cuuint64_t)HD, 16, (cuuint64_t)num_pages * num_kv_heads};
-    const cuuint64_t pstr[2] = {(cuuint64_t)HD * 2, (cuuint64_t)16 * HD * 2};
-    const cuuint32_t pbox[3] = {64, 16, 1};
-    int rc = encode_bf16_map(&mq, q, 3, qdims, qstr, qbox);
-    if (rc) return rc;
-    rc = encode_bf16_map(&mk, k_pages, 3, pdims, pstr, pbox);
-    if (rc) return rc;
-    rc = encode_bf16_map(&mv, v_pages, 3, pdims, pstr, pbox);
-    if (rc) return rc;
-    static bool attr_set = false;
-    if (!attr_set) {
-        LF_CHECK_CUDA(cudaFuncSetAttribute(attn2_kernel<Mode::Paged>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
-        attr_set = true;
-    }
     Params p{};
     p.c = scale * kLog2e;
     p.o = o;
@@ -123,12 +159,9 @@ extern "C" int lf_prefill_paged_fwd(const lf_bf16* q, const lf_bf16* k_pages,
     p.max_pages = max_pages;
     p.max_pairs = (int)max_pairs;
     p.n_items = (int)n_items;
-    int sms = 0;
-    LF_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0));
-    const long grid = n_items < sms ? n_items : sms;
-    attn2_kernel<Mode::Paged><<<(unsigned)grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
-        mq, mk, mv, p);
-    return launch_status("prefill paged");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    return head_dim == 128 ? launch_paged<128>(q, k_pages, v_pages, total_q, p, n_items, st)
+                           : launch_paged<64>(q, k_pages, v_pages, total_q, p, n_items, st);
 }
 
 namespace lf {
@@ -146,6 +179,7 @@ int launch_prefix_tc(const uint16_t* q, const uint16_t* kp, const uint16_t* vp, 
     LF_CHECK_ARG(G >= 1 && G <= 8 && (G & (G - 1)) == 0, "decode prefix: Hq/Hkv must be 1, 2, 4 or 8");
     CUtensorMap mq, mk, mv;
     // q [N][Hkv][G][D]: box = 128/G sessions x G heads x 64 dims of one KV head.
+    constexpr int HD = 128;
     const cuuint64_t qdims[4] = {(cuuint64_t)HD, (cuuint64_t)G, (cuuint64_t)Hkv, (cuuint64_t)N};
     const cuuint64_t qstr[3] = {(cuuint64_t)HD * 2, (cuuint64_t)G * HD * 2, (cuuint64_t)Hq * HD * 2};
     const cuuint32_t qbox[4] = {64, (cuuint32_t)G, 1, (cuuint32_t)(BM / G)};
@@ -162,7 +196,7 @@ int launch_prefix_tc(const uint16_t* q, const uint16_t* kp, const uint16_t* vp, 
 
     static bool attr_set = false;
     if (!attr_set) {
-        LF_CHECK_CUDA(cudaFuncSetAttribute(attn2_kernel<Mode::Prefix>,
+        LF_CHECK_CUDA(cudaFuncSetAttribute(attn2_kernel<Mode::Prefix, 128>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
         attr_set = true;
     }
@@ -187,9 +221,10 @@ int launch_prefix_tc(const uint16_t* q, const uint16_t* kp, const uint16_t* vp, 
     LF_CHECK_ARG(n_items < 2147483647L, "decode prefix: too many work items");
     p.n_items = (int)n_items;
     int sms = 0;
-    LF_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0));
+    rc = sm_count(&sms);
+    if (rc) return rc;
     const long grid = n_items < sms ? n_items : sms;
-    attn2_kernel<Mode::Prefix><<<(unsigned)grid, kThreads, kSmemBytes, st>>>(mq, mk, mv, p);
+    attn2_kernel<Mode::Prefix, 128><<<(unsigned)grid, kThreads, kSmemBytes, st>>>(mq, mk, mv, p);
     return launch_status("decode prefix (tensor cores)");
 }
 

@@ -14,8 +14,8 @@ pytestmark = pytest.mark.gpu
 TOL_MAX, TOL_MEAN = 2e-2, 2e-3
 
 
-def _run_and_check(B, Hq, Hkv, Sq, Sk, causal, seed=0):
-    q, k, v = prefill_inputs(B, Hq, Hkv, Sq, 128, seed=seed, Sk=Sk)
+def _run_and_check(B, Hq, Hkv, Sq, Sk, causal, seed=0, D=128):
+    q, k, v = prefill_inputs(B, Hq, Hkv, Sq, D, seed=seed, Sk=Sk)
     o, lse = att.prefill_attention_fwd(q, k, v, causal=causal, return_lse=True)
     ref, ref_lse = ora.prefill(q.cpu(), k.cpu(), v.cpu(), causal=causal)
     d = (o.float().cpu() - ref).abs()
@@ -44,6 +44,12 @@ def test_prefill_gqa_noncausal():
 def test_prefill_appended_queries(Sq, Sk):
     """Bottom-right causal: new tool-output tokens attend to a cached prefix."""
     _run_and_check(1, 4, 1, Sq, Sk, True, seed=Sq + Sk)
+
+
+@pytest.mark.parametrize("Sq,Sk,causal", [(200, 200, True), (128, 512, True), (77, 300, False)])
+def test_prefill_head_dim_64(Sq, Sk, causal):
+    """GPT-2 style 64-dim heads (MHA 12 heads)."""
+    _run_and_check(1, 12, 12, Sq, Sk, causal, seed=Sq, D=64)
 
 
 def test_prefill_longer_sequence():

@@ -20,10 +20,10 @@ def _rand(*shape, g):
     return torch.randn(*shape, generator=g, device="cuda", dtype=torch.float32).bfloat16()
 
 
-@pytest.mark.parametrize("hq,hkv", [(32, 8), (8, 8)])
-def test_paged_prefill_matches_oracle(hq, hkv):
+@pytest.mark.parametrize("hq,hkv,D", [(32, 8, 128), (8, 8, 128), (12, 12, 64), (16, 4, 64)])
+def test_paged_prefill_matches_oracle(hq, hkv, D):
     g = torch.Generator(device="cuda").manual_seed(11)
-    L, D = 2, 128
+    L = 2
     pool = KVPool(num_layers=L, num_heads=hq, num_kv_heads=hkv, head_dim=D, max_seq_len=2048,
                   max_slots=6, dtype=torch.bfloat16)
     base = pool.allocate_slot()
