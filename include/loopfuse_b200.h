@@ -214,6 +214,53 @@ int lf_pool_read(const lf_pool_meta* m, int seq, int layer, int start, int end,
                  const void* k_pages, const void* v_pages, void* k_out, void* v_out,
                  int num_layers, int num_kv_heads, int head_dim, void* stream);
 
+/* ---- prefix-hash dedup (KV fusion by content) ------------------------------------------
+ * The reference's KV fusion is a compile-time pass keyed on IR positions
+ * (passes/kv_fusion.py:80-107) and its pool has no sharing (runtime/kv_pool.py:28-235), so
+ * these have no reference counterpart; they are the device side of the pool's dedup path.
+ * A full page of 16 tokens is named by a chained 64-bit hash,
+ *   local_j = FNV-1a-64 over the little-endian bytes of its 16 int32 token ids,
+ *   h_j     = fmix64(h_{j-1} ^ local_j)   (h_{-1} = 0; a result of 0 becomes 1),
+ * so a page's hash covers every token before it.  The registry is an open-addressing table
+ * (linear probing, key 0 = empty) of `capacity` (a power of two) entries in device memory,
+ * filled to at most capacity / 2; it holds one refcount on every registered page.  At most
+ * LF_MAX_DEDUP_PAGES pages of a session are hashed.  Errors go to the pool's sticky status
+ * (LF_EINVAL bad session / non-empty dedup destination, LF_ENOPAGES registry full). */
+#define LF_MAX_DEDUP_PAGES 4096
+
+typedef struct lf_prefix_registry {
+    unsigned long long* keys; /* [capacity]; 0 = empty */
+    int32_t* pages;           /* [capacity] page id of each key */
+    int32_t* used;            /* [1] entries in use */
+    int capacity;             /* power of two */
+} lf_prefix_registry;
+
+/* Empty the table (no refcounts are touched: use lf_pool_unregister_all first). */
+int lf_registry_init(const lf_prefix_registry* r, void* stream);
+
+/* Chained page hashes of `n_tokens` token ids: out[j] for the n_tokens / 16 full pages
+ * (at most LF_MAX_DEDUP_PAGES). */
+int lf_prefix_hashes(const int32_t* tokens, int n_tokens, unsigned long long* out, void* stream);
+
+/* Register the full pages of session `seq` whose token ids are `tokens` (the first
+ * min(n_tokens, len(seq)) tokens count): every page whose hash is not yet in the registry is
+ * added with one more reference.  All or nothing on LF_ENOPAGES.  *added (device, nullable)
+ * receives the number of pages added. */
+int lf_pool_register_prefix(const lf_pool_meta* m, const lf_prefix_registry* r, int seq,
+                            const int32_t* tokens, int n_tokens, int32_t* added, void* stream);
+
+/* For each of `n` distinct empty sessions, map the longest run of leading full pages whose
+ * hashes are registered (session i's tokens are tokens[cu_tokens[i] .. cu_tokens[i+1]]) onto
+ * the registered pages (refcount += 1) and set its length to the tokens covered, also written
+ * to covered[i] (device, nullable).  One CTA per session. */
+int lf_pool_dedup_prefix(const lf_pool_meta* m, const lf_prefix_registry* r,
+                         const int32_t* seq_ids, const int32_t* tokens, const int32_t* cu_tokens,
+                         int n, int32_t* covered, void* stream);
+
+/* Drop the registry's references and empty it; pages reaching refcount 0 re-enter the free
+ * queue tail in ascending page-id order. */
+int lf_pool_unregister_all(const lf_pool_meta* m, const lf_prefix_registry* r, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -32,6 +32,13 @@ class PoolMeta(ctypes.Structure):
                 ("page_size", c_int32)]
 
 
+LF_MAX_DEDUP_PAGES = 4096
+
+
+class PrefixRegistry(ctypes.Structure):
+    _fields_ = [("keys", c_void_p), ("pages", c_void_p), ("used", c_void_p), ("capacity", c_int)]
+
+
 _P = c_void_p
 # name -> argtypes (all functions return int unless listed in _RESTYPE)
 _SIGS = {
@@ -58,6 +65,11 @@ _SIGS = {
     "lf_pool_gather": [POINTER(PoolMeta), _P, c_int, _P, c_int, _P, _P],
     "lf_pool_read": [POINTER(PoolMeta), c_int, c_int, c_int, c_int, _P, _P, _P, _P, c_int, c_int,
                      c_int, _P],
+    "lf_registry_init": [POINTER(PrefixRegistry), _P],
+    "lf_prefix_hashes": [_P, c_int, _P, _P],
+    "lf_pool_register_prefix": [POINTER(PoolMeta), POINTER(PrefixRegistry), c_int, _P, c_int, _P, _P],
+    "lf_pool_dedup_prefix": [POINTER(PoolMeta), POINTER(PrefixRegistry), _P, _P, _P, c_int, _P, _P],
+    "lf_pool_unregister_all": [POINTER(PoolMeta), POINTER(PrefixRegistry), _P],
 }
 _RESTYPE = {"lf_version": c_char_p, "lf_last_error": c_char_p}
 

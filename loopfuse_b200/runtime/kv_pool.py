@@ -13,10 +13,12 @@ error behaviour but stores K/V in 16-token pages that sessions can share:
   copy, since pages are not contiguous).
 * New paged API: ``alloc``, ``append`` (batched), ``fork`` (share a prefix by
   reference), ``free``, ``block_table`` (batch table for ``paged_decode``),
-  ``layer_pages``, ``snapshot``.
+  ``layer_pages``, ``snapshot``, and content-addressed sharing:
+  ``register_prefix`` / ``dedup_prefix`` / ``unregister_all`` (a device hash
+  registry of full pages keyed by the chained hash of their token ids).
 
-Every metadata operation (page allocation, fork, free, block-table gather) is
-a device kernel from ``liblf_sm100.so`` launched on the pool's stream; no
+Every metadata operation (page allocation, fork, free, block-table gather,
+prefix-hash register / dedup) is a device kernel from ``liblf_sm100.so`` launched on the pool's stream; no
 CPU-side page bookkeeping exists.  K/V storage is ``[L, P, Hkv, 16, D]`` per
 tensor: one layer's pages are ``[P, Hkv, 16, D]``, a page of one head 4 KB
 contiguous at D = 128.
@@ -34,6 +36,20 @@ from .. import _lib
 from .._lib import LF_PAGE_SIZE, LoopfuseError, PoolMeta
 
 _DTYPES = {"bf16": torch.bfloat16, "fp16": torch.float16}
+
+
+def prefix_hashes(tokens: torch.Tensor) -> torch.Tensor:
+    """Chained 64-bit hashes (as int64) of the full 16-token pages of a CUDA int32 token
+    vector, computed on the device: the keys ``KVPool.register_prefix`` / ``dedup_prefix``
+    use.  At most ``LF_MAX_DEDUP_PAGES`` pages."""
+    if tokens.device.type != "cuda" or tokens.dtype != torch.int32:
+        raise LoopfuseError(_lib.LF_EINVAL, "prefix_hashes: tokens must be a CUDA int32 tensor")
+    toks = tokens.reshape(-1).contiguous()
+    n = min(toks.numel() // LF_PAGE_SIZE, _lib.LF_MAX_DEDUP_PAGES)
+    out = torch.empty(n, dtype=torch.int64, device=toks.device)
+    _lib.call("lf_prefix_hashes", toks.data_ptr(), toks.numel(), out.data_ptr(),
+              torch.cuda.current_stream(toks.device).cuda_stream)
+    return out
 
 
 class KVState:
@@ -105,6 +121,7 @@ class KVPool:
         self._active: Dict[int, KVState] = {}
         self._write_count = 0
         self._bytes_written = 0
+        self._reg: Optional[_lib.PrefixRegistry] = None
         with torch.cuda.device(dev):
             self._call("lf_pool_init", self._meta_ref(), self._stream())
 
@@ -372,6 +389,60 @@ class KVPool:
         for s in states:
             del self._active[s.slot_id]
             self._free_slots.append(s.slot_id)
+
+    # -- prefix-hash dedup (content-addressed KV fusion) ----------------------------------
+    def _registry(self) -> "_lib.PrefixRegistry":
+        if self._reg is None:
+            cap = 1 << max(10, (2 * self.num_pages - 1).bit_length())
+            self._reg_keys = torch.zeros(cap, dtype=torch.int64, device=self.device)
+            self._reg_pages = torch.empty(cap, dtype=torch.int32, device=self.device)
+            self._reg_used = torch.zeros(1, dtype=torch.int32, device=self.device)
+            self._reg = _lib.PrefixRegistry(self._reg_keys.data_ptr(), self._reg_pages.data_ptr(),
+                                            self._reg_used.data_ptr(), cap)
+            self._call("lf_registry_init", _lib.ctypes.byref(self._reg), self._stream())
+        return self._reg
+
+    def _tokens(self, tokens) -> torch.Tensor:
+        return torch.as_tensor(tokens, dtype=torch.int32).reshape(-1).to(self.device)
+
+    def register_prefix(self, state: KVState, tokens) -> int:
+        """Publish the session's full pages under the chained hash of their token ids (the
+        first ``state.current_len`` of ``tokens`` count); returns pages added (host sync)."""
+        toks = self._tokens(tokens)
+        added = torch.zeros(1, dtype=torch.int32, device=self.device)
+        reg = self._registry()
+        self._call("lf_pool_register_prefix", self._meta_ref(), _lib.ctypes.byref(reg),
+                   state.slot_id, toks.data_ptr(), toks.numel(), added.data_ptr(), self._stream())
+        self._raise_if_failed("register_prefix", "prefix registry full or bad session")
+        return int(added.item())
+
+    def dedup_prefix(self, states: Sequence[KVState], tokens: Sequence) -> List[int]:
+        """Map each (empty) session's longest registered run of leading full pages onto the
+        registered pages; returns the tokens each one now holds (host sync)."""
+        states = list(states)
+        if not states:
+            return []
+        chunks = [self._tokens(t) for t in tokens]
+        cu = torch.tensor([0] + [int(c.numel()) for c in chunks], dtype=torch.int64).cumsum(0)
+        toks = torch.cat(chunks) if chunks else torch.empty(0, dtype=torch.int32, device=self.device)
+        ids = self._ids([s.slot_id for s in states])
+        cu_d = cu.to(torch.int32).to(self.device)
+        covered = torch.zeros(len(states), dtype=torch.int32, device=self.device)
+        reg = self._registry()
+        self._call("lf_pool_dedup_prefix", self._meta_ref(), _lib.ctypes.byref(reg), ids.data_ptr(),
+                   toks.data_ptr(), cu_d.data_ptr(), len(states), covered.data_ptr(), self._stream())
+        self._raise_if_failed("dedup_prefix", "destinations must be distinct empty sessions")
+        out = covered.tolist()
+        for s, n in zip(states, out):
+            s.current_len = n
+        return out
+
+    def unregister_all(self) -> None:
+        """Drop the registry's page references and empty it."""
+        if self._reg is None:
+            return
+        self._call("lf_pool_unregister_all", self._meta_ref(), _lib.ctypes.byref(self._reg),
+                   self._stream())
 
     def block_table(self, states: Sequence[KVState], max_pages: Optional[int] = None
                     ) -> Tuple[torch.Tensor, torch.Tensor]:

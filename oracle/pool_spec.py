@@ -47,10 +47,16 @@ initially ``0, 1, ..., P-1``.
     Full pages are identified by a chained 64-bit hash of their token ids
     (``page_hash``).  ``register`` records, for each full page of a session,
     hash -> page (first writer wins; the registry holds one reference, so a
-    registered page is not freed until ``unregister_all``).  ``dedup`` maps
-    the longest run of leading full pages of a new (empty) session whose
-    hashes are registered onto those pages (refcount += 1) and returns the
-    number of tokens it covered.
+    registered page is not freed until ``unregister_all``).  The registry
+    holds at most ``registry_capacity // 2`` entries: a ``register`` that
+    would pass that adds nothing (ENOPAGES).  ``dedup`` maps the longest run
+    of leading full pages of a new (empty) session whose hashes are
+    registered onto those pages (refcount += 1) and returns the number of
+    tokens it covered; ``dedup_many`` does that for a batch of distinct empty
+    sessions (all or nothing on EINVAL).  ``unregister_all`` drops the
+    registry's references; pages reaching zero re-enter the queue tail in
+    ascending page-id order.  Both consider at most ``MAX_DEDUP_PAGES`` pages
+    of a session.
 """
 from __future__ import annotations
 
@@ -64,6 +70,8 @@ OK = 0
 EINVAL = 1
 ENOPAGES = 2
 EOVERFLOW = 3
+
+MAX_DEDUP_PAGES = 4096
 
 _MASK64 = (1 << 64) - 1
 _FNV_OFFSET = 0xCBF29CE484222325
@@ -82,21 +90,25 @@ def _fmix64(h: int) -> int:
     return h
 
 
-def page_hash(prev: int, tokens: Sequence[int]) -> int:
-    """Chained hash of one full page of token ids.
-
-    FNV-1a over the little-endian bytes of ``prev`` and of each 32-bit token
-    id, then ``fmix64``.  The first page of a session chains from ``prev = 0``.
-    The device kernel computes the same function.
-    """
+def page_local_hash(tokens: Sequence[int]) -> int:
+    """FNV-1a (64-bit) over the little-endian bytes of one page's 32-bit token ids."""
     h = _FNV_OFFSET
-    for b in int(prev & _MASK64).to_bytes(8, "little"):
-        h = ((h ^ b) * _FNV_PRIME) & _MASK64
     for t in tokens:
         for b in int(t & 0xFFFFFFFF).to_bytes(4, "little"):
             h = ((h ^ b) * _FNV_PRIME) & _MASK64
-    h = _fmix64(h)
-    return h if h != 0 else 1          # 0 marks an empty registry slot
+    return h
+
+
+def page_hash(prev: int, tokens: Sequence[int]) -> int:
+    """Chained hash of one full page: ``fmix64(prev ^ page_local_hash(tokens))``.
+
+    The first page of a session chains from ``prev = 0``, so a page's hash covers every token
+    before it.  The per-page FNV part has no dependence on ``prev`` (the device computes it for
+    all pages in parallel); only the cheap ``fmix64`` step is serial.  0 marks an empty
+    registry slot, so a hash of 0 becomes 1.
+    """
+    h = _fmix64((prev ^ page_local_hash(tokens)) & _MASK64)
+    return h if h != 0 else 1
 
 
 class PoolError(RuntimeError):
@@ -110,8 +122,10 @@ class PagedKVPoolSpec:
 
     def __init__(self, num_pages: int, max_seqs: int, max_pages_per_seq: int,
                  num_layers: int = 0, num_kv_heads: int = 0, head_dim: int = 0,
-                 dtype: torch.dtype = torch.bfloat16, with_data: bool = False):
+                 dtype: torch.dtype = torch.bfloat16, with_data: bool = False,
+                 registry_capacity: int = 4096):
         self.num_pages = num_pages
+        self.registry_capacity = registry_capacity
         self.max_seqs = max_seqs
         self.max_pages_per_seq = max_pages_per_seq
         self.free_queue: List[int] = list(range(num_pages))
@@ -242,43 +256,56 @@ class PagedKVPoolSpec:
     # -- prefix-hash dedup ------------------------------------------------
     def hashes(self, tokens: Sequence[int]) -> List[int]:
         out, h = [], 0
-        for j in range(len(tokens) // PAGE):
+        for j in range(min(len(tokens) // PAGE, MAX_DEDUP_PAGES)):
             h = page_hash(h, tokens[j * PAGE:(j + 1) * PAGE])
             out.append(h)
         return out
 
     def register(self, seq: int, tokens: Sequence[int]) -> int:
         """Record hash -> page for the session's full pages; returns pages added."""
-        added = 0
-        for j, h in enumerate(self.hashes(tokens[: self.seq_len[seq]])):
-            if h not in self.registry:
-                p = self.block_table[seq][j]
-                self.registry[h] = p
-                self.refcount[p] += 1
-                added += 1
-        return added
+        if not 0 <= seq < self.max_seqs:
+            raise PoolError(EINVAL, f"register: bad session {seq}")
+        hs = self.hashes(tokens[: self.seq_len[seq]])[: self.max_pages_per_seq]
+        new = [j for j, h in enumerate(hs) if h not in self.registry]
+        if len(self.registry) + len(new) > self.registry_capacity // 2:
+            raise PoolError(ENOPAGES, "prefix registry full")
+        for j in new:
+            p = self.block_table[seq][j]
+            self.registry[hs[j]] = p
+            self.refcount[p] += 1
+        return len(new)
 
     def dedup(self, seq: int, tokens: Sequence[int]) -> int:
         """Share the longest registered run of leading full pages; returns tokens covered."""
-        if self.seq_len[seq] != 0:
+        return self.dedup_many([seq], [tokens])[0]
+
+    def dedup_many(self, seqs: Sequence[int], tokens: Sequence[Sequence[int]]) -> List[int]:
+        if len(set(seqs)) != len(seqs) or any(
+                not 0 <= s < self.max_seqs or self.seq_len[s] != 0 for s in seqs):
             raise PoolError(EINVAL, "dedup destination is not empty")
-        n = 0
-        for j, h in enumerate(self.hashes(tokens)):
-            if j >= self.max_pages_per_seq or h not in self.registry:
-                break
-            p = self.registry[h]
-            self.block_table[seq][j] = p
-            self.refcount[p] += 1
-            n += 1
-        self.seq_len[seq] = n * PAGE
-        return n * PAGE
+        out = []
+        for seq, toks in zip(seqs, tokens):
+            n = 0
+            for j, h in enumerate(self.hashes(toks)):
+                if j >= self.max_pages_per_seq or h not in self.registry:
+                    break
+                p = self.registry[h]
+                self.block_table[seq][j] = p
+                self.refcount[p] += 1
+                n += 1
+            self.seq_len[seq] = n * PAGE
+            out.append(n * PAGE)
+        return out
 
     def unregister_all(self) -> None:
-        """Drop the registry's references (pages reaching zero return to the queue)."""
+        """Drop the registry's references (pages reaching zero return to the queue in
+        ascending page-id order)."""
+        freed = []
         for h, p in self.registry.items():
             self.refcount[p] -= 1
             if self.refcount[p] == 0:
-                self.free_queue.append(p)
+                freed.append(p)
+        self.free_queue.extend(sorted(freed))
         self.registry.clear()
 
     # -- snapshot ---------------------------------------------------------

@@ -136,3 +136,31 @@ def test_prefix_hash_dedup():
     sp.close_seq(b)
     sp.unregister_all()
     assert sorted(sp.free_queue) == list(range(32))
+
+
+def test_dedup_registry_capacity_and_order():
+    """Registry limit is capacity // 2 (all or nothing); unregister frees in page order."""
+    sp = PagedKVPoolSpec(num_pages=16, max_seqs=3, max_pages_per_seq=8, registry_capacity=8)
+    a = sp.open_seq()
+    sp.reserve([a], [80])                             # 5 pages: more than the limit of 4
+    toks = list(range(80))
+    before = sp.snapshot()
+    with pytest.raises(PoolError) as e:
+        sp.register(a, toks)
+    assert e.value.code == ENOPAGES and sp.snapshot() == before and not sp.registry
+    sp.close_seq(a)
+    a = sp.open_seq()
+    sp.reserve([a], [64])                             # pages popped after the 5 freed
+    assert sp.register(a, toks) == 4
+    b, c = sp.open_seq(), sp.open_seq()
+    assert sp.dedup_many([b, c], [toks[:64], toks[:20] + [9] * 40]) == [64, 16]
+    with pytest.raises(PoolError):
+        sp.dedup_many([b], [toks])                    # not empty
+    sp.close_seq(a)
+    sp.close_seq(b)
+    sp.close_seq(c)
+    q0 = len(sp.free_queue)
+    sp.unregister_all()
+    tail = sp.free_queue[q0:]
+    assert tail == sorted(tail) and len(tail) == 4
+    _check_invariants(sp)
