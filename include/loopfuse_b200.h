@@ -214,6 +214,24 @@ int lf_pool_read(const lf_pool_meta* m, int seq, int layer, int start, int end,
                  const void* k_pages, const void* v_pages, void* k_out, void* v_out,
                  int num_layers, int num_kv_heads, int head_dim, void* stream);
 
+/* Fused QKV epilogue of one layer (replaces kernels/cuda/ring_kv_cache.cu:69-109
+ * ring_kv_write_kernel plus the model's split / rotate / copy steps).  `qkv` is the QKV
+ * projection output, [total_tokens] rows of `qkv_row_stride` bf16 elements, each row q heads
+ * (num_q_heads x head_dim), then k heads, then v heads (num_kv_heads x head_dim each); sessions
+ * back to back as in lf_pool_write_kv (seq_ids, start_pos from lf_pool_reserve, cu_tokens).
+ * q and k are rotated ("rotate half" RoPE, out[i] = x[i]c - x[i+D/2]s, out[i+D/2] =
+ * x[i+D/2]c + x[i]s, fp32 without FMA contraction, rounded to bf16) with c, s =
+ * rope_cos/rope_sin[pos][i] from [rope_rows][head_dim/2] fp32 tables, pos = the token's
+ * position in its session; NULL tables skip the rotation.  q goes to q_out [total_tokens,
+ * num_q_heads, head_dim]; k and v go to this layer's pages (k_pages, v_pages: [P, Hkv, 16, D]).
+ * head_dim a multiple of 16; all buffers 16-byte aligned.  A position past the table or a
+ * missing page sets the pool's sticky status to LF_EINVAL. */
+int lf_pool_write_qkv(const lf_pool_meta* m, const int32_t* seq_ids, const int32_t* start_pos,
+                      const int32_t* cu_tokens, int n, int total_tokens, const void* qkv,
+                      int64_t qkv_row_stride, const float* rope_cos, const float* rope_sin,
+                      int rope_rows, void* q_out, void* k_pages, void* v_pages, int num_q_heads,
+                      int num_kv_heads, int head_dim, void* stream);
+
 /* ---- prefix-hash dedup (KV fusion by content) ------------------------------------------
  * The reference's KV fusion is a compile-time pass keyed on IR positions
  * (passes/kv_fusion.py:80-107) and its pool has no sharing (runtime/kv_pool.py:28-235), so

@@ -4,8 +4,9 @@ The reference names GPT-2 small as its CPU-runnable program (``ir/dialect.py:525
 d_model 768, 12 heads of 64, ffn 3072, vocab 50257) and runs it through
 ``scaled_dot_product_attention`` (``passes/phase_select.py:80-89``).  Here the attention is the
 package's own: ``prefill_paged`` (tcgen05 core, 64-dim heads, one KV head per query head) for a
-chunk of new tokens over the session's cached pages, ``paged_decode`` for one token.  K/V go to a
-bf16 ``KVPool`` layer by layer.  The dense parts (embeddings, LayerNorm, QKV / output / MLP
+chunk of new tokens over the session's cached pages, ``paged_decode`` for one token.  Each
+layer's QKV output is split by the fused ``KVPool.write_qkv`` kernel: q contiguous, K/V into
+the bf16 pool pages.  The dense parts (embeddings, LayerNorm, QKV / output / MLP
 projections, GELU-tanh) are torch ops in ``dense_dtype`` (fp32 by default, so that the only
 reduced-precision step is the bf16 attention).
 
@@ -114,10 +115,9 @@ class GPT2Model:
         x = w["wte"][tokens.to(self.device)] + w["wpe"][pos]
         for l in range(c.layers):
             h = self._ln(x, f"{l}.ln_1")
-            qkv = h @ w[f"{l}.attn.w"] + w[f"{l}.attn.b"]
-            q, k, v = (t.reshape(T, c.heads, c.head_dim).to(torch.bfloat16).contiguous()
-                       for t in qkv.split(c.d_model, dim=-1))
-            pool.write_layer(states, start, l, k, v, counts, index=index)
+            qkv = (h @ w[f"{l}.attn.w"] + w[f"{l}.attn.b"]).to(torch.bfloat16)
+            q = torch.empty((T, c.heads, c.head_dim), dtype=torch.bfloat16, device=self.device)
+            pool.write_qkv(states, start, l, qkv, q, counts, index=index)   # no rotary in GPT-2
             kp, vp = pool.layer_pages(l)
             if decode:
                 a = att.paged_decode(q, kp, vp, table, lens, num_prefix_pages=n_prefix_pages,

@@ -3,11 +3,13 @@
 Weights are random (N(0, 0.02), bf16): the agent-loop workload measures throughput, and no
 checkpoint is available.  Shapes: 32 layers, d_model 4096, 32 query / 8 KV heads of 128, SwiGLU
 FFN 14336, vocab 128256, RoPE theta 500000, RMSNorm eps 1e-5.  The dense projections are plain
-library GEMMs (``torch.matmul`` -> cuBLAS bf16); normalisation, rotary embedding and the SwiGLU
-gate are elementwise torch ops.  Attention is the package's own: ``prefill_paged`` for a batch of
+library GEMMs (``torch.matmul`` -> cuBLAS bf16); normalisation and the SwiGLU gate are
+elementwise torch ops.  The QKV GEMM's output goes through one fused kernel
+(``KVPool.write_qkv``): split, rotary embedding of q and k from a cached cos/sin table, q
+written contiguous, k and v scattered into the session's pages.  Attention is the package's own: ``prefill_paged`` for a batch of
 new prompt / tool-output tokens over each session's cached pages, ``paged_decode`` (with the
 forked shared prefix read once per group of sessions) for one token per session.  New K/V are
-appended to the pool layer by layer (``KVPool.reserve`` once per forward, ``write_layer`` per
+appended to the pool layer by layer (``KVPool.reserve`` once per forward, ``write_qkv`` per
 layer).
 
 ``forward(tokens, pool, states, counts)`` advances every listed session by ``counts[i]`` tokens
@@ -74,6 +76,18 @@ class LlamaShaped:
         self.inv_freq = 1.0 / (c.rope_theta ** (torch.arange(0, c.head_dim, 2, device=self.device,
                                                                dtype=torch.float32) / c.head_dim))
         self._ws: Optional[torch.Tensor] = None
+        self._rope_rows = 0
+        self._cos = self._sin = None
+        self.fused_qkv = True          # False: the unfused torch split / rotate / pool write path
+
+    def rope_tables(self, rows: int):
+        """``[rows, D/2]`` fp32 cos / sin of position x inverse frequency (grown on demand)."""
+        if rows > self._rope_rows:
+            rows = max(rows, 2 * self._rope_rows, 4096)
+            ang = torch.arange(rows, device=self.device).float()[:, None] * self.inv_freq[None, :]
+            self._cos, self._sin = ang.cos().contiguous(), ang.sin().contiguous()
+            self._rope_rows = rows
+        return self._cos, self._sin
 
     def param_bytes(self) -> int:
         ts = [self.embed, self.lm_head] + self.wqkv + self.wo + self.w13 + self.w2
@@ -109,10 +123,13 @@ class LlamaShaped:
         start = pool.reserve(states, counts)
         index = pool.batch_index(states, counts)
         table, lens = pool.block_table(states)
-        pos = torch.cat([torch.arange(s0, s0 + n, device=self.device) for s0, n in
-                         zip(starts_host, counts)]).float()
-        ang = pos[:, None] * self.inv_freq[None, :]
-        cos, sin = ang.cos()[:, None, :], ang.sin()[:, None, :]
+        if self.fused_qkv:
+            rope = self.rope_tables(max(s0 + n for s0, n in zip(starts_host, counts)))
+        else:
+            pos = torch.cat([torch.arange(s0, s0 + n, device=self.device) for s0, n in
+                             zip(starts_host, counts)]).float()
+            ang = pos[:, None] * self.inv_freq[None, :]
+            cos, sin = ang.cos()[:, None, :], ang.sin()[:, None, :]
         decode = all(n == 1 for n in counts)
         if not decode:
             cu = torch.tensor([0] + list(torch.tensor(counts).cumsum(0)), dtype=torch.int32,
@@ -128,17 +145,21 @@ class LlamaShaped:
         for l in range(c.layers):
             h = self._rmsnorm(x, self.attn_norm[l])
             qkv = h @ self.wqkv[l]
-            q = self._rope(qkv[:, :nq].view(T, c.q_heads, c.head_dim), cos, sin)
-            k = self._rope(qkv[:, nq:nq + nk].view(T, c.kv_heads, c.head_dim), cos, sin)
-            v = qkv[:, nq + nk:].reshape(T, c.kv_heads, c.head_dim).contiguous()
-            pool.write_layer(states, start, l, k.contiguous(), v, counts, index=index)
+            if self.fused_qkv:
+                q = torch.empty((T, c.q_heads, c.head_dim), dtype=qkv.dtype, device=self.device)
+                pool.write_qkv(states, start, l, qkv, q, counts, rope=rope, index=index)
+            else:
+                q = self._rope(qkv[:, :nq].view(T, c.q_heads, c.head_dim), cos, sin).contiguous()
+                k = self._rope(qkv[:, nq:nq + nk].view(T, c.kv_heads, c.head_dim), cos, sin)
+                v = qkv[:, nq + nk:].reshape(T, c.kv_heads, c.head_dim).contiguous()
+                pool.write_layer(states, start, l, k.contiguous(), v, counts, index=index)
             kp, vp = pool.layer_pages(l)
             if decode:
-                a = att.paged_decode(q.contiguous(), kp, vp, table, lens,
+                a = att.paged_decode(q, kp, vp, table, lens,
                                      num_prefix_pages=n_prefix_pages, pages_per_split=pps,
                                      workspace=self._ws)
             else:
-                a = att.prefill_paged(q.contiguous(), kp, vp, table, cu, lens, max(counts))
+                a = att.prefill_paged(q, kp, vp, table, cu, lens, max(counts))
             x = x + a.view(T, nq) @ self.wo[l]
             h = self._rmsnorm(x, self.ffn_norm[l])
             gu = h @ self.w13[l]

@@ -390,6 +390,46 @@ class KVPool:
             del self._active[s.slot_id]
             self._free_slots.append(s.slot_id)
 
+    def write_qkv(self, states: Sequence[KVState], start: torch.Tensor, layer: int,
+                  qkv: torch.Tensor, q_out: torch.Tensor, counts: Sequence[int],
+                  rope: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+                  stream: Optional[torch.cuda.Stream] = None, index=None) -> None:
+        """Fused QKV epilogue of one layer: ``qkv [T_total, (Hq + 2 Hkv) * D]`` (q heads, then
+        k heads, then v heads per row; rows may be strided) is split, q and k are rotated with
+        ``rope = (cos, sin)`` tables ``[rows, D/2]`` fp32 indexed by each token's position in
+        its session ("rotate half" form; None skips it), q goes to ``q_out [T_total, Hq, D]``
+        and k, v to this layer's pages -- one kernel."""
+        ids, cu_t, total = index if index is not None else self.batch_index(states, counts)
+        if total == 0:
+            return
+        Hq, Hkv, D = q_out.shape[1], self.num_kv_heads, self.head_dim
+        if qkv.dtype != self.dtype or qkv.device != self.device or qkv.dim() != 2 or \
+                qkv.shape[0] != total or qkv.shape[1] != (Hq + 2 * Hkv) * D or qkv.stride(1) != 1:
+            raise LoopfuseError(_lib.LF_EINVAL, "write_qkv expects qkv [T_total, (Hq+2Hkv)*D] "
+                                                "rows of the pool dtype")
+        if q_out.dtype != self.dtype or not q_out.is_contiguous() or \
+                tuple(q_out.shape) != (total, Hq, D):
+            raise LoopfuseError(_lib.LF_EINVAL, "write_qkv: q_out must be contiguous [T, Hq, D]")
+        cos = sin = None
+        rows = 0
+        if rope is not None:
+            cos, sin = rope
+            for t in (cos, sin):
+                if t.dtype != torch.float32 or not t.is_contiguous() or t.dim() != 2 or \
+                        t.shape[1] != D // 2 or t.device != self.device:
+                    raise LoopfuseError(_lib.LF_EINVAL, "write_qkv: rope tables must be "
+                                                        "contiguous fp32 [rows, D/2] on the pool device")
+            rows = cos.shape[0]
+        elem = self.keys.element_size()
+        layer_off = layer * self.keys.stride(0) * elem
+        self._call("lf_pool_write_qkv", self._meta_ref(), ids.data_ptr(), start.data_ptr(),
+                   cu_t.data_ptr(), len(states), total, qkv.data_ptr(), qkv.stride(0),
+                   cos.data_ptr() if cos is not None else None,
+                   sin.data_ptr() if sin is not None else None, rows, q_out.data_ptr(),
+                   self.keys.data_ptr() + layer_off, self.values.data_ptr() + layer_off, Hq, Hkv, D,
+                   self._stream(stream))
+        self._bytes_written += 2 * total * Hkv * D * elem
+
     # -- prefix-hash dedup (content-addressed KV fusion) ----------------------------------
     def _registry(self) -> "_lib.PrefixRegistry":
         if self._reg is None:
