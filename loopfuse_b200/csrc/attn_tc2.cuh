@@ -91,8 +91,9 @@ struct Params {
     float* part_o;
     float2* part_ml;
     int N, G, num_pages, max_pages, n_prefix, chunk_pages, n_chunks, n_qtiles, n_slots, slot0;
+    // G: prefix mode -- the GQA group; paged mode -- query heads packed per work item
     const int32_t* cu_q;     // paged: [N+1] query row offsets
-    int max_pairs;           // paged: tile pairs of the longest query run
+    int max_pairs;           // paged: tile pairs of the longest packed query run
 };
 
 struct Item {
@@ -112,22 +113,26 @@ __device__ __forceinline__ Item item_coords(const Params& p, int w, int lane) {
     it.q_row0[0] = it.q_row0[1] = 0;
     it.sess = it.q_tok0 = it.lq = it.lk = 0;
     if constexpr (M == Mode::Paged) {
-        const int pair = p.max_pairs - 1 - w / (p.N * p.Hq);   // heavy pairs first
-        const int rest = w % (p.N * p.Hq);
-        it.sess = rest / p.Hq;
-        it.bhq = rest % p.Hq;                                   // query head
-        it.kvh = it.bhq / (p.Hq / p.Hkv);
+        // GQA packing: the p.G query heads of a group share one K/V stream; packed row r of a
+        // (session, group) is token r / p.G, head group * p.G + r % p.G.
+        const int NG = p.Hq / p.G;
+        const int pair = p.max_pairs - 1 - w / (p.N * NG);      // heavy pairs first
+        const int rest = w % (p.N * NG);
+        it.sess = rest / NG;
+        it.bhq = rest % NG;                                     // query group
+        it.kvh = it.bhq * p.G / (p.Hq / p.Hkv);
         it.q_tok0 = p.cu_q[it.sess];
         it.lq = p.cu_q[it.sess + 1] - it.q_tok0;
         it.lk = min(max(p.lens[it.sess], 0), p.max_pages * 16);
         it.p_end = (it.lk + 15) / 16;
+        const int rows = it.lq * p.G;
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
             it.q_row0[t] = (2 * pair + t) * BM;
             int n = 0;
-            if (it.q_row0[t] < it.lq) {
+            if (it.q_row0[t] < rows) {
                 int kv_end = it.lk;
-                if (p.causal) kv_end = min(it.lk, it.q_row0[t] + BM + (it.lk - it.lq));
+                if (p.causal) kv_end = min(it.lk, (it.q_row0[t] + BM) / p.G + (it.lk - it.lq));
                 n = kv_end > 0 ? (kv_end + BN - 1) / BN : 0;
             }
             it.nb[t] = n;
@@ -248,8 +253,8 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                             if constexpr (M == Mode::Dense) {
                                 tma_load_3d(dst, &tmq, bar(Q_FULL), hf * 64, it.q_row0[t], it.bhq);
                             } else if constexpr (M == Mode::Paged) {
-                                tma_load_3d(dst, &tmq, bar(Q_FULL), hf * 64, it.bhq,
-                                            it.q_tok0 + it.q_row0[t]);
+                                tma_load_4d(dst, &tmq, bar(Q_FULL), hf * 64, 0, it.bhq,
+                                            it.q_tok0 + it.q_row0[t] / p.G);
                             } else {
                                 tma_load_4d(dst, &tmq, bar(Q_FULL), hf * 64, 0, it.h,
                                             it.n0 + t * (BM / p.G));
@@ -261,18 +266,29 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                 if constexpr (M == Mode::Prefix) bt_row = p.bt + (size_t)it.src * p.max_pages;
                 if constexpr (M == Mode::Paged) bt_row = p.bt + (size_t)it.sess * p.max_pages;
                 const int kv_head = (M == Mode::Paged) ? it.kvh : it.h;
+                // Page ids of one 128-key block: 8 independent loads issued together, fetched
+                // one block ahead (their latency overlaps the wait for a free stage) and shared
+                // by the K and V copies.
+                int ids[8];
+                auto fetch_ids = [&](int j) {
+#pragma unroll
+                    for (int pg = 0; pg < 8; ++pg) {
+                        const int pi = it.p_begin + j * 8 + pg;
+                        ids[pg] = pi < it.p_end ? __ldg(bt_row + pi) : -1;
+                    }
+                };
                 auto load_kv = [&](const CUtensorMap* map, uint32_t dst, uint32_t full, int j) {
                     if constexpr (M == Mode::Dense) {
 #pragma unroll
                         for (int hf = 0; hf < HD / 64; ++hf)
                             tma_load_3d(dst + hf * kHalfBytes, map, full, hf * 64, j * BN, it.kvh);
                     } else {
-#pragma unroll 1
+#pragma unroll
                         for (int pg = 0; pg < 8; ++pg) {
                             const int pi = it.p_begin + j * 8 + pg;
                             int row = p.num_pages * p.Hkv;           // out of range: zeros
                             if (pi < it.p_end) {
-                                const int page = bt_row[pi];
+                                const int page = ids[pg];
                                 if (static_cast<unsigned>(page) >= static_cast<unsigned>(p.num_pages))
                                     atomicCAS(&g_device_error, 0, 201);
                                 else
@@ -285,6 +301,7 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                         }
                     }
                 };
+                if constexpr (M != Mode::Dense) fetch_ids(0);
                 for (int j = 0; ok && j < it.nbk; ++j) {
                     const int gj = g + j, st = gj & 1;
                     const uint32_t ph = (gj >> 1) & 1;
@@ -294,6 +311,8 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                     if (!(ok = mbar_wait(bar(V_EMPTY + st), ph ^ 1, abort_flag, 2))) break;
                     mbar_arrive_expect_tx(bar(V_FULL + st), kLoadBytes);
                     load_kv(&tmv, sbase + OFF_V + st * kTileBytes, bar(V_FULL + st), j);
+                    if constexpr (M != Mode::Dense)
+                        if (j + 1 < it.nbk) fetch_ids(j + 1);
                 }
             }
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -410,7 +429,7 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                 qpos = it.q_row0[t] + row + p.q_offset;
                 key_limit = p.Sk;
             } else if constexpr (M == Mode::Paged) {
-                qpos = it.q_row0[t] + row + (it.lk - it.lq);
+                qpos = (it.q_row0[t] + row) / p.G + (it.lk - it.lq);
                 key_limit = it.lk;
             } else {
                 const int rr = t * BM + row;
@@ -531,12 +550,14 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
             }
             // ---- epilogue: read O_t (the next item's first P.V may then overwrite it) ----
             if constexpr (M != Mode::Prefix) {
-                // dense: o [B*Hq][Sq][D]; paged: o [T_total][Hq][D]; lse alike without D.
+                // dense: o [B*Hq][Sq][D]; paged: o [T_total][Hq][D] from packed rows; lse alike
+                // without D.
                 const int grow = it.q_row0[t] + row;
-                const int rows = (M == Mode::Dense) ? p.Sq : it.lq;
+                const int rows = (M == Mode::Dense) ? p.Sq : it.lq * p.G;
                 const size_t orow = (M == Mode::Dense)
                                         ? static_cast<size_t>(it.bhq) * p.Sq + grow
-                                        : (static_cast<size_t>(it.q_tok0) + grow) * p.Hq + it.bhq;
+                                        : (static_cast<size_t>(it.q_tok0) + grow / p.G) * p.Hq +
+                                              static_cast<size_t>(it.bhq) * p.G + grow % p.G;
                 if (it.q_row0[t] < rows) {
                     const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
 #pragma unroll 1

@@ -65,13 +65,15 @@ int launch_paged(const lf_bf16* q, const lf_bf16* kp, const lf_bf16* vp, int tot
                  long n_items, cudaStream_t st) {
     using namespace lf::tc2;
     CUtensorMap mq, mk, mv;
-    const cuuint64_t qdims[3] = {(cuuint64_t)HD, (cuuint64_t)p.Hq, (cuuint64_t)total_q};
-    const cuuint64_t qstr[2] = {(cuuint64_t)HD * 2, (cuuint64_t)p.Hq * HD * 2};
-    const cuuint32_t qbox[3] = {64, 1, 128};
+    // q [total_q][Hq / G][G][HD]: one box = 128 / G tokens x the G heads of one group.
+    const cuuint64_t qdims[4] = {(cuuint64_t)HD, (cuuint64_t)p.G, (cuuint64_t)(p.Hq / p.G),
+                                 (cuuint64_t)total_q};
+    const cuuint64_t qstr[3] = {(cuuint64_t)HD * 2, (cuuint64_t)p.G * HD * 2, (cuuint64_t)p.Hq * HD * 2};
+    const cuuint32_t qbox[4] = {64, (cuuint32_t)p.G, 1, (cuuint32_t)(BM / p.G)};
     const cuuint64_t pdims[3] = {(cuuint64_t)HD, 16, (cuuint64_t)p.num_pages * p.Hkv};
     const cuuint64_t pstr[2] = {(cuuint64_t)HD * 2, (cuuint64_t)16 * HD * 2};
     const cuuint32_t pbox[3] = {64, 16, 1};
-    int rc = lf::encode_bf16_map(&mq, q, 3, qdims, qstr, qbox);
+    int rc = lf::encode_bf16_map(&mq, q, 4, qdims, qstr, qbox);
     if (rc) return rc;
     rc = lf::encode_bf16_map(&mk, kp, 3, pdims, pstr, pbox);
     if (rc) return rc;
@@ -141,8 +143,12 @@ extern "C" int lf_prefill_paged_fwd(const lf_bf16* q, const lf_bf16* k_pages,
     LF_CHECK_ARG(num_seqs > 0 && total_q > 0 && max_seqlen_q > 0 && num_kv_heads > 0 &&
                      num_q_heads % num_kv_heads == 0 && num_pages > 0 && max_pages > 0,
                  "prefill paged: bad sizes");
-    const long max_pairs = ((max_seqlen_q + BM - 1) / BM + 1) / 2;
-    const long n_items = max_pairs * num_seqs * num_q_heads;
+    // GQA packing: the query heads of a KV group share a work item (and its K/V stream) when
+    // the group size divides the 128-row tile; otherwise every head is its own group.
+    const int group = num_q_heads / num_kv_heads;
+    const int pack = (BM % group == 0) ? group : 1;
+    const long max_pairs = (((long)max_seqlen_q * pack + BM - 1) / BM + 1) / 2;
+    const long n_items = max_pairs * num_seqs * (num_q_heads / pack);
     LF_CHECK_ARG(n_items < 2147483647L, "prefill paged: too many work items");
     Params p{};
     p.c = scale * kLog2e;
@@ -155,6 +161,7 @@ extern "C" int lf_prefill_paged_fwd(const lf_bf16* q, const lf_bf16* k_pages,
     p.lens = seqlens_k;
     p.cu_q = cu_seqlens_q;
     p.N = num_seqs;
+    p.G = pack;
     p.num_pages = num_pages;
     p.max_pages = max_pages;
     p.max_pairs = (int)max_pairs;

@@ -20,7 +20,8 @@ def _rand(*shape, g):
     return torch.randn(*shape, generator=g, device="cuda", dtype=torch.float32).bfloat16()
 
 
-@pytest.mark.parametrize("hq,hkv,D", [(32, 8, 128), (8, 8, 128), (12, 12, 64), (16, 4, 64)])
+@pytest.mark.parametrize("hq,hkv,D", [(32, 8, 128), (8, 8, 128), (12, 12, 64), (16, 4, 64),
+                                      (12, 4, 128), (32, 4, 128), (32, 2, 64)])
 def test_paged_prefill_matches_oracle(hq, hkv, D):
     g = torch.Generator(device="cuda").manual_seed(11)
     L = 2
