@@ -246,6 +246,7 @@ def run_agent(args):
                                             seed=args.seed + 99), device=grp.device)
     warm.run()
     del warm
+    loop.setup()                     # system prompt prefill + fork source, decode graph capture
     torch.cuda.synchronize()
     grp.barrier()
     st = loop.run()
@@ -264,7 +265,8 @@ def run_agent(args):
                           "prefill_batches": st.prefill_batches, "prefill_tokens": st.prefill_tokens,
                           "decode_iters": st.decode_iters, "decode_tokens": st.decode_tokens,
                           "spec_batches": st.spec_batches, "spec_tokens": st.spec_tokens,
-                          "idle_waits": st.idle_waits,
+                          "idle_waits": st.idle_waits, "prefill_s": round(st.prefill_s, 3),
+                          "decode_s": round(st.decode_s, 3), "spec_s": round(st.spec_s, 3),
                           "model_tflops": round(model.flops_per_token() *
                                                 (st.prefill_tokens + st.decode_tokens) /
                                                 st.gpu_busy_s / 1e12, 1) if st.gpu_busy_s else None},

@@ -232,6 +232,21 @@ int lf_pool_write_qkv(const lf_pool_meta* m, const int32_t* seq_ids, const int32
                       int rope_rows, void* q_out, void* k_pages, void* v_pages, int num_q_heads,
                       int num_kv_heads, int head_dim, void* stream);
 
+/* ---- decoder elementwise ops around the attention path ---------------------------------
+ * Residual add + RMSNorm, one CTA per row (the norm half of kernels/triton/fused_ln_qkv.py:27-72,
+ * whose LayerNorm stays in registers ahead of the QKV product; here the norm is RMSNorm and the
+ * residual add is fused in instead).  For each of `rows` contiguous rows of `dim` bf16:
+ * if delta != NULL, x = bf16(x + delta) in place; then if w != NULL,
+ * out = bf16(bf16(x * r) * w) with r = 1 / sqrt(mean(x^2) + eps).  dim a multiple of 8, at most
+ * 8192; buffers 16-byte aligned. */
+int lf_add_rmsnorm(lf_bf16* x, const lf_bf16* delta, const lf_bf16* w, lf_bf16* out, int rows,
+                   int dim, float eps, void* stream);
+
+/* SwiGLU gate of a fused gate|up projection gu [rows, 2*ffn] bf16:
+ * out[r][j] = bf16(bf16(silu(gu[r][j])) * gu[r][ffn + j]), out [rows, ffn].  No reference
+ * counterpart (the reference models are GPT-style). */
+int lf_swiglu(const lf_bf16* gu, lf_bf16* out, int rows, int ffn, void* stream);
+
 /* ---- prefix-hash dedup (KV fusion by content) ------------------------------------------
  * The reference's KV fusion is a compile-time pass keyed on IR positions
  * (passes/kv_fusion.py:80-107) and its pool has no sharing (runtime/kv_pool.py:28-235), so

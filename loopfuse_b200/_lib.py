@@ -67,6 +67,8 @@ _SIGS = {
                      c_int, _P],
     "lf_pool_write_qkv": [POINTER(PoolMeta), _P, _P, _P, c_int, c_int, _P, c_int64, _P, _P, c_int,
                           _P, _P, _P, c_int, c_int, c_int, _P],
+    "lf_add_rmsnorm": [_P, _P, _P, _P, c_int, c_int, c_float, _P],
+    "lf_swiglu": [_P, _P, c_int, c_int, _P],
     "lf_registry_init": [POINTER(PrefixRegistry), _P],
     "lf_prefix_hashes": [_P, c_int, _P, _P],
     "lf_pool_register_prefix": [POINTER(PoolMeta), POINTER(PrefixRegistry), c_int, _P, c_int, _P, _P],

@@ -18,8 +18,10 @@ Scheduling (one host thread per GPU, a loop of GPU batches):
      ("Observation:"), so while a session's tool runs, those ``spec_tokens`` tokens are
      prefilled ahead of time (on the pool's low-priority stream); when the tool returns only
      the tool output itself is left to prefill.
-The system prompt (``prefix_tokens``) is prefilled once and forked to every session, so the
-decode attention reads it once per group of sessions.
+The system prompt (``prefix_tokens``) is prefilled once (``setup``, before the loop) and forked
+to every session, so the decode attention reads it once per group of sessions.  Decode
+iterations replay CUDA graphs (``llama.GraphedDecode``), one per batch-size bucket, captured in
+``setup``; prefill batches run eagerly.
 
 Token ids are synthetic (seeded uniform ids; tool outputs of geometric length, mean
 ``tool_len_mean``, capped).  The reported metric is agent steps per second: completed ReAct
@@ -35,7 +37,7 @@ from typing import Dict, List, Optional
 import numpy as np
 import torch
 
-from .llama import LlamaShaped
+from .llama import GraphedDecode, LlamaShaped
 from .runtime.kv_pool import KVPool, KVState
 
 PAGE = 16
@@ -53,6 +55,7 @@ class AgentLoopConfig:
     tool_len_cap: int = 1024
     spec_tokens: int = 4
     speculative: bool = True
+    graphs: bool = True              # decode iterations replayed from CUDA graphs
     max_prefill_tokens: int = 16384
     seed: int = 0
 
@@ -84,6 +87,9 @@ class AgentLoopStats:
     prefill_tokens: int = 0
     decode_tokens: int = 0
     gpu_busy_s: float = 0.0
+    prefill_s: float = 0.0
+    decode_s: float = 0.0
+    spec_s: float = 0.0
     idle_waits: int = 0
 
 
@@ -108,9 +114,11 @@ class AgentLoop:
         pages = self.n_prefix_pages + sum((o + PAGE - 1) // PAGE + 1 for o in own) + 16
         mc = model.cfg
         self.pool = KVPool(num_layers=mc.layers, num_heads=mc.q_heads, num_kv_heads=mc.kv_heads,
-                           head_dim=mc.head_dim, max_seq_len=max_len, max_slots=n + 1,
-                           dtype=torch.bfloat16, device=self.device, num_pages=pages)
+                           head_dim=mc.head_dim, max_seq_len=max_len, max_slots=n + 2,
+                           dtype=torch.bfloat16, device=self.device, num_pages=pages + 1)
         self.rng = np.random.default_rng(cfg.seed + 17)
+        self.root: Optional[KVState] = None
+        self.gd: Optional[GraphedDecode] = None
 
     def _ids_tensor(self, toks: List[int]) -> torch.Tensor:
         return torch.tensor(toks, dtype=torch.long).to(self.device, non_blocking=True)
@@ -124,14 +132,37 @@ class AgentLoop:
         stats.gpu_busy_s += time.perf_counter() - t0
         return out
 
+    def setup(self) -> None:
+        """System prompt prefilled once into a root session (forked to every session when the
+        loop runs); with ``graphs``, a padding session and the decode graphs of every batch
+        bucket up to the session count."""
+        cfg, pool = self.cfg, self.pool
+        self.root = pool.alloc()
+        sys_prompt = [int(x) for x in self.rng.integers(0, self.vocab, size=cfg.prefix_tokens)]
+        self._run([_Sess(-1, self.root)], [sys_prompt], AgentLoopStats())
+        if cfg.graphs:
+            pad = pool.pad_session(self.root, cfg.prefix_tokens)
+            self.gd = GraphedDecode(self.model, pool, pad, self.n_prefix_pages)
+            self.gd.prepare(len(self.ids))
+        torch.cuda.synchronize(self.device)
+
+    def _decode(self, sess: List[_Sess], stats: AgentLoopStats) -> List[int]:
+        if self.gd is None:
+            return self._run(sess, [[s.last_token] for s in sess], stats)
+        t0 = time.perf_counter()
+        nxt = self.gd.step([s.state for s in sess], [s.last_token for s in sess])
+        out = nxt[:len(sess)].tolist()
+        self.gd.raise_if_failed()
+        stats.gpu_busy_s += time.perf_counter() - t0
+        return out
+
     def run(self) -> AgentLoopStats:
         cfg, pool = self.cfg, self.pool
+        if self.root is None:
+            self.setup()
         stats = AgentLoopStats(sessions=len(self.ids))
         t_start = time.perf_counter()
-        # shared system prompt, prefilled once, forked to every session
-        root = pool.alloc()
-        sys_prompt = [int(x) for x in self.rng.integers(0, self.vocab, size=cfg.prefix_tokens)]
-        self._run([_Sess(-1, root)], [sys_prompt], stats)
+        root = self.root
         states = pool.fork(root, cfg.prefix_tokens, n=len(self.ids))
         sessions = [_Sess(i, st, k) for k, (i, st) in enumerate(zip(self.ids, states))]
         for s in sessions:
@@ -155,7 +186,9 @@ class AgentLoop:
                         break
                     batch.append(s)
                     budget -= len(s.pending)
+                t0 = time.perf_counter()
                 nxt = self._run(batch, [s.pending for s in batch], stats)
+                stats.prefill_s += time.perf_counter() - t0
                 stats.prefill_batches += 1
                 stats.prefill_tokens += sum(len(s.pending) for s in batch)
                 for s, t in zip(batch, nxt):
@@ -163,7 +196,9 @@ class AgentLoop:
                     s.spec_done = False
                 continue
             if dec:
-                nxt = self._run(dec, [[s.last_token] for s in dec], stats)
+                t0 = time.perf_counter()
+                nxt = self._decode(dec, stats)
+                stats.decode_s += time.perf_counter() - t0
                 stats.decode_iters += 1
                 stats.decode_tokens += len(dec)
                 now = time.perf_counter()
@@ -185,9 +220,11 @@ class AgentLoop:
             # idle window: speculative prefill of the observation template
             spec = [s for s in sessions if s.phase == "tool" and not s.spec_done] if cfg.speculative else []
             if spec:
+                t0 = time.perf_counter()
                 with torch.cuda.stream(pool.prefetch_stream):
                     self._run(spec, [list(self.template) for _ in spec], stats)
                 torch.cuda.current_stream().wait_stream(pool.prefetch_stream)
+                stats.spec_s += time.perf_counter() - t0
                 for s in spec:
                     s.spec_done = True
                 stats.spec_batches += 1
@@ -198,5 +235,5 @@ class AgentLoop:
         torch.cuda.synchronize(self.device)
         stats.wall_s = time.perf_counter() - t_start
         stats.steps_per_s = stats.steps_done / stats.wall_s
-        pool.release_all(states + [root])
+        pool.release_all(states)
         return stats

@@ -23,7 +23,9 @@ from typing import List, Optional, Sequence
 import torch
 import torch.nn.functional as F
 
+from . import _lib
 from . import attention as att
+from . import model_ops as mo
 from .runtime.kv_pool import KVPool, KVState
 
 
@@ -78,11 +80,15 @@ class LlamaShaped:
         self._ws: Optional[torch.Tensor] = None
         self._rope_rows = 0
         self._cos = self._sin = None
+        self._rope_old: list = []      # replaced tables stay alive: captured graphs point at them
         self.fused_qkv = True          # False: the unfused torch split / rotate / pool write path
+        self.fused_ops = True          # False: torch RMSNorm / residual adds / SwiGLU
 
     def rope_tables(self, rows: int):
         """``[rows, D/2]`` fp32 cos / sin of position x inverse frequency (grown on demand)."""
         if rows > self._rope_rows:
+            if self._cos is not None:
+                self._rope_old.append((self._cos, self._sin))
             rows = max(rows, 2 * self._rope_rows, 4096)
             ang = torch.arange(rows, device=self.device).float()[:, None] * self.inv_freq[None, :]
             self._cos, self._sin = ang.cos().contiguous(), ang.sin().contiguous()
@@ -110,6 +116,24 @@ class LlamaShaped:
         xf = x.float()
         x1, x2 = xf[..., :half], xf[..., half:]
         return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1).to(x.dtype)
+
+    def _norm_in(self, x: torch.Tensor, delta: Optional[torch.Tensor], w: Optional[torch.Tensor]):
+        """``x += delta``; returns ``rmsnorm(x) * w`` (None when ``w`` is None)."""
+        if self.fused_ops:
+            return mo.add_rmsnorm(x, delta, w, self.cfg.eps)
+        if delta is not None:
+            x.add_(delta)
+        return self._rmsnorm(x, w) if w is not None else None
+
+    def _mlp_block(self, x: torch.Tensor, attn: torch.Tensor, l: int):
+        """Rest of layer ``l`` after attention: output projection, residual, FFN norm, SwiGLU
+        FFN, residual, and the next layer's input norm.  Returns (x, normed input of l + 1)."""
+        c = self.cfg
+        h = self._norm_in(x, attn @ self.wo[l], self.ffn_norm[l])
+        gu = h @ self.w13[l]
+        act = mo.swiglu(gu) if self.fused_ops else F.silu(gu[:, :c.ffn]) * gu[:, c.ffn:]
+        nxt = self.attn_norm[l + 1] if l + 1 < c.layers else None
+        return x, self._norm_in(x, act @ self.w2[l], nxt)
 
     # -- forward ------------------------------------------------------------------------------
     @torch.no_grad()
@@ -142,8 +166,8 @@ class LlamaShaped:
                 self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
         x = self.embed[tokens]
         nq, nk = c.q_heads * c.head_dim, c.kv_heads * c.head_dim
+        h = self._norm_in(x, None, self.attn_norm[0])
         for l in range(c.layers):
-            h = self._rmsnorm(x, self.attn_norm[l])
             qkv = h @ self.wqkv[l]
             if self.fused_qkv:
                 q = torch.empty((T, c.q_heads, c.head_dim), dtype=qkv.dtype, device=self.device)
@@ -160,12 +184,9 @@ class LlamaShaped:
                                      workspace=self._ws)
             else:
                 a = att.prefill_paged(q, kp, vp, table, cu, lens, max(counts))
-            x = x + a.view(T, nq) @ self.wo[l]
-            h = self._rmsnorm(x, self.ffn_norm[l])
-            gu = h @ self.w13[l]
-            x = x + (F.silu(gu[:, :c.ffn]) * gu[:, c.ffn:]) @ self.w2[l]
+            x, h = self._mlp_block(x, a.view(T, nq), l)
         last = torch.tensor(counts, device=self.device).cumsum(0) - 1
-        h = self._rmsnorm(x[last], self.final_norm)
+        h = self._norm_in(x[last].contiguous(), None, self.final_norm)
         logits = h @ self.lm_head
         return logits.float() if return_logits else torch.argmax(logits, dim=-1)
 
@@ -177,3 +198,127 @@ class LlamaShaped:
     def decode(self, tokens: torch.Tensor, kv_state: KVState, attention=None) -> torch.Tensor:
         nxt = self.forward(tokens.to(self.device).long(), kv_state.pool, [kv_state], [1])
         return torch.nn.functional.one_hot(nxt, self.cfg.vocab).float()
+
+
+_BUCKETS = (16, 32, 64, 96, 128, 192, 256, 320, 384, 448, 512)
+
+
+def _bucket(n: int) -> int:
+    for b in _BUCKETS:
+        if n <= b:
+            return b
+    return -(-n // 128) * 128
+
+
+class GraphedDecode:
+    """One-token decode steps replayed from CUDA graphs, one graph per batch-size bucket.
+
+    A decode step of the model is ~700 kernel launches, so at small batches the host's launch
+    rate, not the GPU, sets the step time.  Here a step is: one pinned host -> device copy of
+    (tokens, slot ids, counts), one graph replay (pool reserve and block-table gather, every
+    layer, final norm, LM head, argmax), and the caller's read of the result.  A batch of n
+    sessions runs in the graph of the smallest bucket >= n; rows past n take 0 new tokens in
+    ``pad`` (a ``KVPool.pad_session``): their pages never grow and their outputs are ignored.
+    Each graph has its own memory pool; the pool's device status is copied back with the
+    output (``raise_if_failed`` after the caller's sync).
+    """
+
+    def __init__(self, model: "LlamaShaped", pool: KVPool, pad: KVState, n_prefix_pages: int = 0):
+        self.model, self.pool, self.pad, self.npp = model, pool, pad, n_prefix_pages
+        self.graphs = {}
+        self.status_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+
+    def _build(self, nb: int):
+        m, pool, dev = self.model, self.pool, self.model.device
+        c = m.cfg
+        s = {"nb": nb,
+             "host": torch.zeros((3, nb), dtype=torch.int32, pin_memory=True),
+             "dev": torch.zeros((3, nb), dtype=torch.int32, device=dev),
+             "cu": torch.arange(nb + 1, dtype=torch.int32, device=dev),
+             "start": torch.zeros(nb, dtype=torch.int32, device=dev),
+             "table": torch.empty((nb, pool.max_pages_per_seq), dtype=torch.int32, device=dev),
+             "lens": torch.empty(nb, dtype=torch.int32, device=dev),
+             "copied": torch.cuda.Event()}
+        s["pps"] = att.default_pages_per_split(nb, c.kv_heads, pool.max_pages_per_seq)
+        s["ws"] = torch.empty(att.decode_workspace_bytes(nb, c.q_heads, c.head_dim,
+                                                         pool.max_pages_per_seq, s["pps"], self.npp),
+                              dtype=torch.uint8, device=dev)
+        # rows: real sessions take 1 token; a fresh graph's warm-up runs every row as padding
+        s["host"][1].fill_(self.pad.slot_id)
+        s["dev"].copy_(s["host"])
+        m.rope_tables(pool.max_seq_len + 1)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            self._body(s)                          # warm-up outside capture (allocator, cuBLAS)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            s["out"] = self._body(s)
+        s["graph"] = g
+        return s
+
+    @torch.no_grad()
+    def _body(self, s) -> torch.Tensor:
+        m, pool = self.model, self.pool
+        c = m.cfg
+        nb = s["nb"]
+        toks, ids, cnt = s["dev"][0], s["dev"][1], s["dev"][2]
+        pool.reserve_device(ids, cnt, s["start"], nb)
+        pool.gather_device(ids, nb, s["table"], s["lens"])
+        rope = (m._cos, m._sin)
+        index = (ids, s["cu"], nb)
+        x = m.embed[toks.long()]
+        nq = c.q_heads * c.head_dim
+        h = m._norm_in(x, None, m.attn_norm[0])
+        for l in range(c.layers):
+            qkv = h @ m.wqkv[l]
+            q = torch.empty((nb, c.q_heads, c.head_dim), dtype=qkv.dtype, device=m.device)
+            pool.write_qkv(None, s["start"], l, qkv, q, None, rope=rope, index=index)
+            kp, vp = pool.layer_pages(l)
+            a = att.paged_decode(q, kp, vp, s["table"], s["lens"], num_prefix_pages=self.npp,
+                                 pages_per_split=s["pps"], workspace=s["ws"])
+            x, h = m._mlp_block(x, a.view(nb, nq), l)
+        return torch.argmax(m._norm_in(x, None, m.final_norm) @ m.lm_head, dim=-1)
+
+    def prepare(self, max_batch: int) -> None:
+        """Capture the graphs of every bucket up to ``max_batch`` sessions."""
+        for b in _BUCKETS:
+            if b not in self.graphs:
+                self.graphs[b] = self._build(b)
+            if b >= max_batch:
+                break
+
+    def step(self, states: Sequence[KVState], tokens: Sequence[int]) -> torch.Tensor:
+        """Advance each session by its token; returns the device tensor of greedy next tokens
+        (the first ``len(states)`` rows are valid)."""
+        n = len(states)
+        nb = _bucket(n)
+        s = self.graphs.get(nb)
+        if s is None:
+            s = self.graphs[nb] = self._build(nb)
+        for st in states:
+            if st.current_len + 1 > self.pool.max_seq_len:
+                raise RuntimeError(f"KV cache overflow: current_len={st.current_len} + seq_new=1 > "
+                                   f"max_seq_len={self.pool.max_seq_len}")
+        s["copied"].synchronize()                  # the previous copy out of this buffer is done
+        host = s["host"]
+        host[0, :n] = torch.as_tensor(list(tokens), dtype=torch.int32)
+        host[1, :n] = torch.as_tensor([st.slot_id for st in states], dtype=torch.int32)
+        host[2, :n] = 1
+        host[0, n:] = 0
+        host[1, n:] = self.pad.slot_id
+        host[2, n:] = 0
+        s["dev"].copy_(host, non_blocking=True)
+        s["copied"].record()
+        s["graph"].replay()
+        self.status_host.copy_(self.pool._ctrl[_lib.LF_CTRL_STATUS:_lib.LF_CTRL_STATUS + 1],
+                               non_blocking=True)
+        for st in states:
+            st.current_len += 1
+        return s["out"]
+
+    def raise_if_failed(self) -> None:
+        """Call after a sync that follows ``step`` (e.g. reading its output)."""
+        if int(self.status_host[0]) != _lib.LF_OK:
+            self.pool._raise_if_failed("graphed decode")

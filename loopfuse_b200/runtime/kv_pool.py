@@ -390,6 +390,28 @@ class KVPool:
             del self._active[s.slot_id]
             self._free_slots.append(s.slot_id)
 
+    # -- device-buffer forms (no host bookkeeping, no sync: usable inside CUDA-graph capture) --
+    def reserve_device(self, slot_ids: torch.Tensor, counts: torch.Tensor, start: torch.Tensor,
+                       n: int) -> None:
+        """``lf_pool_reserve`` on device int32 buffers of ``n`` entries.  The caller keeps the
+        host ``KVState.current_len`` in step and reads ``status()`` when it next syncs."""
+        self._call("lf_pool_reserve", self._meta_ref(), slot_ids.data_ptr(), counts.data_ptr(), n,
+                   start.data_ptr(), self._stream())
+
+    def gather_device(self, slot_ids: torch.Tensor, n: int, table: torch.Tensor,
+                      lens: torch.Tensor) -> None:
+        """Block-table rows and lengths of ``n`` slots into ``table [n, W]`` / ``lens [n]``."""
+        self._call("lf_pool_gather", self._meta_ref(), slot_ids.data_ptr(), n, table.data_ptr(),
+                   table.shape[1], lens.data_ptr(), self._stream())
+
+    def pad_session(self, root: Optional[KVState] = None, prefix_len: int = 0) -> KVState:
+        """A session for the padding rows of fixed-size batches: it shares ``root``'s first
+        ``prefix_len`` tokens (when given) and has a free row in its last page, so a batch row
+        that appends 0 tokens can write its K/V at position ``current_len`` harmlessly."""
+        st = self.fork(root, prefix_len, n=1)[0] if root is not None else self.alloc()
+        self.reserve([st], [1 if st.current_len % LF_PAGE_SIZE == 0 else 0])
+        return st
+
     def write_qkv(self, states: Sequence[KVState], start: torch.Tensor, layer: int,
                   qkv: torch.Tensor, q_out: torch.Tensor, counts: Sequence[int],
                   rope: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
@@ -423,7 +445,7 @@ class KVPool:
         elem = self.keys.element_size()
         layer_off = layer * self.keys.stride(0) * elem
         self._call("lf_pool_write_qkv", self._meta_ref(), ids.data_ptr(), start.data_ptr(),
-                   cu_t.data_ptr(), len(states), total, qkv.data_ptr(), qkv.stride(0),
+                   cu_t.data_ptr(), ids.numel(), total, qkv.data_ptr(), qkv.stride(0),
                    cos.data_ptr() if cos is not None else None,
                    sin.data_ptr() if sin is not None else None, rows, q_out.data_ptr(),
                    self.keys.data_ptr() + layer_off, self.values.data_ptr() + layer_off, Hq, Hkv, D,

@@ -73,3 +73,47 @@ def test_small_agent_loop_completes_every_step():
     assert st.steps_done == cfg.sessions * cfg.steps
     assert st.decode_tokens >= cfg.sessions * cfg.steps * (cfg.decode_tokens - 1)
     assert st.steps_per_s > 0
+
+
+def test_graphed_decode_matches_eager_decode():
+    """Graph replays (padded batch buckets) advance the same sessions as eager forwards on the
+    same input tokens: the same pool metadata, next tokens that agree (GEMMs of another batch
+    size may round differently), the sessions' K/V within bf16 rounding."""
+    from loopfuse_b200.llama import GraphedDecode
+    m = LlamaShaped(SMALL, seed=4)
+    runs = []
+    for graphed in (False, True):
+        pool = KVPool(num_layers=SMALL.layers, num_heads=SMALL.q_heads, num_kv_heads=SMALL.kv_heads,
+                      head_dim=SMALL.head_dim, max_seq_len=512, max_slots=24, dtype=torch.bfloat16)
+        root = pool.alloc()
+        g = torch.Generator().manual_seed(5)
+        m.forward(torch.randint(0, SMALL.vocab, (64,), generator=g).cuda(), pool, [root], [64])
+        ss = pool.fork(root, 64, n=20)
+        lens = [int(x) for x in torch.randint(1, 40, (20,), generator=g)]
+        m.forward(torch.randint(0, SMALL.vocab, (sum(lens),), generator=g).cuda(), pool, ss, lens,
+                  n_prefix_pages=4)
+        pad = pool.pad_session(root, 64)
+        gd = GraphedDecode(m, pool, pad, n_prefix_pages=4) if graphed else None
+        outs = []
+        for it in range(6):
+            batch = ss[: 20 - 3 * it]                        # shrinking batch: 20, 17, ..., 5
+            tb = [int(x) for x in torch.randint(0, SMALL.vocab, (len(batch),), generator=g)]
+            if graphed:
+                nxt = gd.step(batch, tb)[: len(batch)].tolist()
+                gd.raise_if_failed()
+            else:
+                nxt = m.forward(torch.tensor(tb, device="cuda"), pool, batch, [1] * len(batch),
+                                n_prefix_pages=4).tolist()
+            outs.append(nxt)
+        snap = pool.snapshot()
+        kv = [torch.cat([pool.read(st, l)[0] for l in range(SMALL.layers)]) for st in ss]
+        runs.append((outs, snap, [st.current_len for st in ss], kv))
+    (o_e, s_e, l_e, k_e), (o_g, s_g, l_g, k_g) = runs
+    assert l_e == l_g
+    assert s_e["block_table"] == s_g["block_table"] and s_e["seq_len"] == s_g["seq_len"]
+    assert s_e["free_queue"] == s_g["free_queue"] and s_e["refcount"] == s_g["refcount"]
+    flat_e = [t for o in o_e for t in o]
+    flat_g = [t for o in o_g for t in o]
+    assert sum(a == b for a, b in zip(flat_e, flat_g)) >= 0.9 * len(flat_e)
+    for a, b in zip(k_e, k_g):                                # the sessions' own K, every layer
+        assert (a.float() - b.float()).abs().max().item() < 0.05
