@@ -74,6 +74,12 @@ constexpr uint32_t OFF_BAR = OFF_V + 2 * kTileBytes;
 constexpr uint32_t kSmemBytes = OFF_BAR + 256 + 1024;
 constexpr uint32_t kColS = 0, kColO = 256, kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;
+// Which exp2 pairs of each group of 8 run as a polynomial on the FMA pipe (bit i: pair i % 8);
+// the rest use the MUFU unit.  Balances the two pipes.
+#ifndef LF_POLY_MASK
+#define LF_POLY_MASK 0x88
+#endif
+constexpr unsigned kPolyMask = LF_POLY_MASK;
 
 enum Bar { Q_FULL = 0, Q_EMPTY = 1, K_FULL = 2, K_EMPTY = 4, V_FULL = 6, V_EMPTY = 8, S_FULL = 10,
            P_FULL = 12, O_DONE = 14, NUM_BARS = 16 };
@@ -443,77 +449,55 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                 if (!ok) break;
                 tc_fence_after();
                 // Visible keys of this block form a prefix [0, lim) of its columns (ragged end
-                // and causal diagonal alike).  Masked blocks are rare: their S row is rewritten
-                // in TMEM with -inf past lim, so the two passes below stay branch-free.
+                // and causal diagonal alike).  The whole 128-column S row comes into registers
+                // with one TMEM round trip; masked blocks (rare) get -inf past lim there.
                 const int kbase = j * BN;
                 int lim = key_limit - kbase;
                 if constexpr (M != Mode::Prefix)
                     if (p.causal) lim = min(lim, qpos - kbase + 1);
-                if (__any_sync(0xffffffffu, lim < BN)) {
-#pragma unroll 1
-                    for (int cc = 0; cc < BN / 32; ++cc) {
-                        uint32_t r[32];
-                        tmem_ld32(s_col + cc * 32, r);
-                        tmem_wait_ld();
-                        const int l = lim - cc * 32;
+                uint32_t r[BN];
+                using Chunk = uint32_t[32];
+                auto chunk = [&](int c) -> Chunk& { return *reinterpret_cast<Chunk*>(r + 32 * c); };
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) r[i] = (i < l) ? r[i] : 0xff800000u;   // -inf
-                        tmem_st32(s_col + cc * 32, r);
-                    }
-                    tmem_wait_st();
+                for (int c = 0; c < BN / 32; ++c) tmem_ld32(s_col + c * 32, chunk(c));
+                tmem_wait_ld();
+                if (__any_sync(0xffffffffu, lim < BN)) {
+#pragma unroll
+                    for (int i = 0; i < BN; ++i) r[i] = (i < lim) ? r[i] : 0xff800000u;   // -inf
                 }
-                // pass 1: row max
                 float mxs[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) mxs[i] = -INFINITY;
-#pragma unroll 1
-                for (int hf = 0; hf < 2; ++hf) {
-                    uint32_t r[32], r2[32];
-                    tmem_ld32(s_col + hf * 64, r);
-                    tmem_ld32(s_col + hf * 64 + 32, r2);
-                    tmem_wait_ld();
+                for (int i = 0; i < 8; ++i) mxs[i] = __uint_as_float(r[i]);
 #pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        mxs[i & 7] = fmaxf(mxs[i & 7], fmaxf(__uint_as_float(r[i]), __uint_as_float(r2[i])));
-                }
+                for (int i = 8; i < BN; ++i) mxs[i & 7] = fmaxf(mxs[i & 7], __uint_as_float(r[i]));
                 const float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
                                        fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
                 const float m_blk = mx * p.c;
                 const float m_new = (m_blk > m_run + kRescaleThreshold) ? m_blk : m_run;
                 const float alpha = (m_new == m_run) ? 1.f : fast_exp2(m_run - m_new);
                 const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-                // pass 2: exp2, row sum, bf16 P over the first 64 columns of this S buffer.
+                // exp2, row sum and bf16 P, packed in place: pair i (columns 2i, 2i+1) becomes
+                // r[i], so P of score columns [0, 128) lands in TMEM columns [0, 64) of this
+                // S buffer.  The pairs kPolyMask selects run on the FMA pipe.
                 const uint64_t c2 = f2_pack(p.c, p.c), nm2 = f2_pack(-m_use, -m_use);
                 uint64_t lsa = f2_pack(0.f, 0.f), lsb = f2_pack(0.f, 0.f);
-#pragma unroll 1
-                for (int hf = 0; hf < 2; ++hf) {
-                    uint32_t r[32], r2[32], pr[32];
-                    tmem_ld32(s_col + hf * 64, r);
-                    tmem_ld32(s_col + hf * 64 + 32, r2);
-                    tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const float2 a = f2_unpack(ffma2(
-                            f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), c2, nm2));
-                        const uint64_t b = ffma2(
-                            f2_pack(__uint_as_float(r2[2 * i]), __uint_as_float(r2[2 * i + 1])), c2, nm2);
-                        const float e0 = fast_exp2(a.x), e1 = fast_exp2(a.y);
-                        float2 f;
-                        if ((i & 1) == 0) {
-                            f = exp2_poly2(b);
-                        } else {
-                            const float2 bv = f2_unpack(b);
-                            f = make_float2(fast_exp2(bv.x), fast_exp2(bv.y));
-                        }
-                        lsa = fadd2(lsa, f2_pack(e0, e1));
-                        lsb = fadd2(lsb, f2_pack(f.x, f.y));
-                        pr[i] = pack_bf16x2(e0, e1);
-                        pr[16 + i] = pack_bf16x2(f.x, f.y);
+                for (int i = 0; i < BN / 2; ++i) {
+                    const uint64_t a = ffma2(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])),
+                                             c2, nm2);
+                    float2 e;
+                    if ((kPolyMask >> (i & 7)) & 1u) {
+                        e = exp2_poly2(a);
+                    } else {
+                        const float2 av = f2_unpack(a);
+                        e = make_float2(fast_exp2(av.x), fast_exp2(av.y));
                     }
-                    // columns [hf*32, hf*32+32) hold P of score columns [hf*64, hf*64+64):
-                    // those scores were read above, so the overwrite is safe.
-                    tmem_st32(s_col + hf * 32, pr);
+                    if (i & 1) lsb = fadd2(lsb, f2_pack(e.x, e.y));
+                    else lsa = fadd2(lsa, f2_pack(e.x, e.y));
+                    r[i] = pack_bf16x2(e.x, e.y);
                 }
+                tmem_st32(s_col, chunk(0));
+                tmem_st32(s_col + 32, chunk(1));
                 const float2 lsv = f2_unpack(fadd2(lsa, lsb));
                 const float lsum = lsv.x + lsv.y;
                 if (j > 0) {
