@@ -62,6 +62,7 @@ def parse_args():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-fusion", action="store_true")
+    ap.add_argument("--no-agent", action="store_true", help="skip the agent-loop sub-object")
     ap.add_argument("--workload", choices=["decode", "agent"], default="decode")
     ap.add_argument("--agent-sessions", type=int, default=512)
     ap.add_argument("--agent-steps", type=int, default=10)
@@ -223,24 +224,22 @@ AGENT_WORKLOAD = ("agent loop: Llama-3-8B-shaped random-init bf16 model (32 laye
                   "observation template in GPU-idle windows")
 
 
-def run_agent(args):
-    """Agent steps per second over all ranks (each rank runs its LPT share of the sessions)."""
+def agent_measure(args, grp) -> dict:
+    """Agent loop over this rank's LPT share of the sessions (weights, warm-up, system prompt
+    and decode graphs before the timed loop); returns the whole-job result (on every rank)."""
     import torch
+    import numpy as np
     from loopfuse_b200.agent_loop import AgentLoop, AgentLoopConfig
     from loopfuse_b200.llama import LlamaConfig, LlamaShaped
-    from loopfuse_b200.runtime.sharding import RankGroup, lpt_assign
-    grp = RankGroup()
-    if grp.device.type == "cuda":
-        torch.cuda.set_device(grp.device)
+    from loopfuse_b200.runtime.sharding import lpt_assign
     cfg = AgentLoopConfig(sessions=args.agent_sessions, steps=args.agent_steps, seed=args.seed)
-    import numpy as np
     rng = np.random.default_rng(cfg.seed)
     work = np.minimum(rng.geometric(1.0 / cfg.tool_len_mean, size=(cfg.sessions, cfg.steps)),
                       cfg.tool_len_cap).sum(axis=1)
     mine = lpt_assign([float(x) for x in work], grp.world)[grp.rank]
     model = LlamaShaped(LlamaConfig(), device=grp.device, seed=args.seed)
     loop = AgentLoop(model, cfg, session_ids=mine, device=grp.device)
-    # warm-up: a short loop on two sessions compiles nothing but touches every code path
+    # warm-up: a short loop on two sessions touches every code path
     warm = AgentLoop(model, AgentLoopConfig(sessions=2, steps=1, prefix_tokens=256,
                                             question_tokens=16, decode_tokens=2, tool_ms=1.0,
                                             seed=args.seed + 99), device=grp.device)
@@ -252,25 +251,45 @@ def run_agent(args):
     st = loop.run()
     wall = grp.max(st.wall_s)
     steps = grp.sum(float(st.steps_done))
+    res = {"metric": "agent steps/s", "value": round(steps / wall, 2), "unit": "steps/s",
+           "n_gpus": grp.world, "steps": int(steps), "wall_s": round(wall, 3),
+           "ms_per_step": round(1000 * wall / max(1.0, steps / grp.world), 3),
+           "scaling": "strong", "workload": AGENT_WORKLOAD, "sessions": cfg.sessions,
+           "steps_per_session": cfg.steps, "sessions_on_rank0": len(mine),
+           "parallelism": f"session-sharded x{grp.world} (LPT on tool-output length)",
+           "rank0": {"wall_s": round(st.wall_s, 3), "gpu_busy_s": round(st.gpu_busy_s, 3),
+                     "prefill_batches": st.prefill_batches, "prefill_tokens": st.prefill_tokens,
+                     "decode_iters": st.decode_iters, "decode_tokens": st.decode_tokens,
+                     "spec_batches": st.spec_batches, "spec_tokens": st.spec_tokens,
+                     "idle_waits": st.idle_waits, "prefill_s": round(st.prefill_s, 3),
+                     "decode_s": round(st.decode_s, 3), "spec_s": round(st.spec_s, 3),
+                     "model_tflops": round(model.flops_per_token() *
+                                           (st.prefill_tokens + st.decode_tokens) /
+                                           st.gpu_busy_s / 1e12, 1) if st.gpu_busy_s else None}}
+    del loop, model
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_agent(args):
+    """Agent steps per second over all ranks (each rank runs its LPT share of the sessions)."""
+    import torch
+    from loopfuse_b200.runtime.sharding import RankGroup
+    grp = RankGroup()
+    if grp.device.type == "cuda":
+        torch.cuda.set_device(grp.device)
+    r = agent_measure(args, grp)
     if grp.rank == 0:
-        line = {"metric": "agent steps/s", "value": round(steps / wall, 2), "unit": "steps/s",
-                "n_gpus": grp.world, "steps": int(steps), "warmup": 1,
-                "ms_per_step": round(1000 * wall / max(1.0, steps / grp.world), 3),
-                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-                "dtype": "bf16", "data": "synthetic token ids, random-init weights",
-                "config": {"workload": AGENT_WORKLOAD, "sessions": cfg.sessions,
-                           "steps_per_session": cfg.steps, "sessions_on_rank0": len(mine),
-                           "parallelism": f"session-sharded x{grp.world} (LPT on tool-output length)"},
-                "rank0": {"wall_s": round(st.wall_s, 3), "gpu_busy_s": round(st.gpu_busy_s, 3),
-                          "prefill_batches": st.prefill_batches, "prefill_tokens": st.prefill_tokens,
-                          "decode_iters": st.decode_iters, "decode_tokens": st.decode_tokens,
-                          "spec_batches": st.spec_batches, "spec_tokens": st.spec_tokens,
-                          "idle_waits": st.idle_waits, "prefill_s": round(st.prefill_s, 3),
-                          "decode_s": round(st.decode_s, 3), "spec_s": round(st.spec_s, 3),
-                          "model_tflops": round(model.flops_per_token() *
-                                                (st.prefill_tokens + st.decode_tokens) /
-                                                st.gpu_busy_s / 1e12, 1) if st.gpu_busy_s else None},
-                "e2e": {"value": round(steps / wall, 2), "unit": "steps/s",
+        line = {"metric": r["metric"], "value": r["value"], "unit": r["unit"],
+                "n_gpus": r["n_gpus"], "steps": r["steps"], "warmup": 1,
+                "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic token ids, random-init weights",
+                "config": {"workload": r["workload"], "sessions": r["sessions"],
+                           "steps_per_session": r["steps_per_session"],
+                           "sessions_on_rank0": r["sessions_on_rank0"],
+                           "parallelism": r["parallelism"]},
+                "rank0": r["rank0"],
+                "e2e": {"value": r["value"], "unit": "steps/s",
                         "h2d_bytes_per_step": None, "d2h_bytes_per_step": None}}
         print(json.dumps(line), flush=True)
     grp.close()
@@ -450,6 +469,12 @@ def main():
         del loop
         torch.cuda.empty_cache()
 
+    # ---------------- agent loop (512 sessions x 10 ReAct steps, Llama-3-8B shapes) ----------
+    agent = None
+    if not args.no_agent:
+        from loopfuse_b200.runtime.sharding import RankGroup
+        agent = agent_measure(args, RankGroup())
+
     # ---------------- CPU baseline (rank 0, N=1) ----------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -489,6 +514,7 @@ def main():
             "clocks": clocks,
             "prefill": prefill,
             "kv_fusion_loop": fusion,
+            "agent_loop": agent,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
