@@ -220,7 +220,7 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
             mbar_init(bar(V_FULL + s), 1);
             mbar_init(bar(V_EMPTY + s), 1);
             mbar_init(bar(S_FULL + s), 1);
-            mbar_init(bar(P_FULL + s), 128);
+            mbar_init(bar(P_FULL + s), 4);           // one arrival per softmax warp
             mbar_init(bar(O_DONE + s), 1);
         }
         *abort_flag = 0;
@@ -486,15 +486,18 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                     const uint64_t a = ffma2(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])),
                                              c2, nm2);
                     float2 e;
+                    uint32_t pb;
                     if ((kPolyMask >> (i & 7)) & 1u) {
                         e = exp2_poly2(a);
+                        pb = pack_bf16x2(e.x, e.y);
                     } else {
                         const float2 av = f2_unpack(a);
                         e = make_float2(fast_exp2(av.x), fast_exp2(av.y));
+                        pb = pack_bf16x2(e.x, e.y);
                     }
                     if (i & 1) lsb = fadd2(lsb, f2_pack(e.x, e.y));
                     else lsa = fadd2(lsa, f2_pack(e.x, e.y));
-                    r[i] = pack_bf16x2(e.x, e.y);
+                    r[i] = pb;
                 }
                 tmem_st32(s_col, chunk(0));
                 tmem_st32(s_col + 32, chunk(1));
@@ -523,7 +526,8 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                 m_run = m_new;
                 tmem_wait_st();
                 tc_fence_before();
-                mbar_arrive(bar(P_FULL + t));
+                __syncwarp();                        // the warp's P rows are all in TMEM
+                if (lane == 0) mbar_arrive(bar(P_FULL + t));
                 ++cnt;
             }
             if (!ok) break;
