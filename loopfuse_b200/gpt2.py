@@ -133,6 +133,14 @@ class GPT2Model:
                 + w[f"{l}.fc2.b"]
         return self._ln(x[last], "ln_f") @ w["wte"].t()
 
+    # -- AgentExecutor model contract ------------------------------------------------------
+    def prefill(self, tokens: torch.Tensor, kv_state: KVState, attention=None) -> torch.Tensor:
+        """Append ``tokens`` to the session; last-position logits ``[1, vocab]``."""
+        return self.forward(tokens.to(self.device).long(), kv_state.pool, [kv_state], [tokens.numel()])
+
+    def decode(self, tokens: torch.Tensor, kv_state: KVState, attention=None) -> torch.Tensor:
+        return self.forward(tokens.to(self.device).long(), kv_state.pool, [kv_state], [1])
+
 
 @dataclass
 class ReactTrace:

@@ -17,6 +17,11 @@ four ``_dispatch_*`` methods are ``pass`` (``:278-281``).  Here:
   speculative pages (``KVPool.fork`` keeps the confirmed prefix shared).
 * ``StepTrace`` keeps the reference's wall-clock fields and adds CUDA-event
   GPU times.
+* A ``KVFuseOp`` (``passes.kv_fusion.KVFusionPass``) arms prefix sharing by
+  content for the program's first prefill: the prompt's leading pages whose
+  token hashes an earlier run registered are mapped onto that run's pages
+  (``KVPool.dedup_prefix``), only the rest is prefilled, and this run's first
+  ``prefix_len`` tokens are registered (``KVPool.register_prefix``).
 
 Model contract (duck-typed): ``model.prefill(tokens, kv_state, attention)``
 appends the tokens' K/V to the pool and returns last-position logits;
@@ -50,6 +55,8 @@ class StepTrace:
     parse_action_ms: float = 0.0
     spec_prefill_ms: float = 0.0
     spec_prefill_hit: bool = False
+    prefill_tokens: int = 0
+    prefix_hit_tokens: int = 0                  # prompt tokens served from shared pages
     total_ms: float = 0.0
     gpu_prefill_ms: float = 0.0
     gpu_decode_ms: float = 0.0
@@ -92,7 +99,7 @@ class AgentExecutor:
 
     def __init__(self, model: Any, kv_pool: KVPool, tools: Dict[str, Callable[[str], str]],
                  target: KernelTarget = KernelTarget.CUDA, device: str = "cuda",
-                 max_decode_tokens: int = 64):
+                 max_decode_tokens: int = 64, prefix_cache: bool = True):
         self.model = model
         self.kv_pool = kv_pool
         self.tools = tools
@@ -102,10 +109,13 @@ class AgentExecutor:
         self._dispatch = self._build_dispatch_table()
         self._last_token: Optional[int] = None
         self._spec: Optional[dict] = None
+        self.prefix_cache = prefix_cache
+        self._fuse_len = 0                          # prefix_len of the program's KVFuseOp
 
     # -- top level -------------------------------------------------------------
     def run(self, prog: AgentProgram, initial_input: str) -> ExecutionResult:
         state = self.kv_pool.allocate_slot()
+        self._fuse_len = 0
         traces: List[StepTrace] = []
         output = ""
         t0 = time.perf_counter()
@@ -152,6 +162,8 @@ class AgentExecutor:
             self._exec_kv_write(op, kv_state)
             trace.kv_write_ms += (time.perf_counter() - t0) * 1000
         elif isinstance(op, KVFuseOp):
+            # Arms the content-addressed prefix sharing of the next (first) prefill.
+            self._fuse_len = int(op.attrs.get("prefix_len", 0))
             trace.kv_write_ms += (time.perf_counter() - t0) * 1000
         elif isinstance(op, SpeculativePrefillOp):
             self._exec_spec_prefill(op, kv_state, prog, step)
@@ -186,8 +198,18 @@ class AgentExecutor:
         if op.phase == Phase.PREFILL:
             tokens = self._prompt_tokens(step, op)
             if not self._consume_speculation(kv_state, tokens, trace):
-                logits = self.model.prefill(tokens, kv_state, kernel)
+                fuse = self.prefix_cache and self._fuse_len >= 16 and kv_state.current_len == 0
+                covered = 0
+                if fuse:
+                    # Leading pages another run already computed; one token is always left to
+                    # prefill, since its logits start the decode.
+                    covered = self.kv_pool.dedup_prefix([kv_state], [tokens[:-1].tolist()])[0]
+                logits = self.model.prefill(tokens[covered:], kv_state, kernel)
                 self._last_token = int(torch.argmax(logits[-1]).item())
+                trace.prefill_tokens += int(tokens.numel()) - covered
+                trace.prefix_hit_tokens += covered
+                if fuse:
+                    self.kv_pool.register_prefix(kv_state, tokens[: self._fuse_len].tolist())
         else:
             last = self._last_token if self._last_token is not None else 0
             out = []
