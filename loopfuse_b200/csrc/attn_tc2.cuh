@@ -268,57 +268,72 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                         }
                     }
                 }
-                const int32_t* bt_row = nullptr;
-                if constexpr (M == Mode::Prefix) bt_row = p.bt + (size_t)it.src * p.max_pages;
-                if constexpr (M == Mode::Paged) bt_row = p.bt + (size_t)it.sess * p.max_pages;
-                const int kv_head = (M == Mode::Paged) ? it.kvh : it.h;
-                // Page ids of one 128-key block: 8 independent loads issued together, fetched
-                // one block ahead (their latency overlaps the wait for a free stage) and shared
-                // by the K and V copies.
-                int ids[8];
-                auto fetch_ids = [&](int j) {
-#pragma unroll
-                    for (int pg = 0; pg < 8; ++pg) {
-                        const int pi = it.p_begin + j * 8 + pg;
-                        ids[pg] = pi < it.p_end ? __ldg(bt_row + pi) : -1;
-                    }
-                };
-                auto load_kv = [&](const CUtensorMap* map, uint32_t dst, uint32_t full, int j) {
-                    if constexpr (M == Mode::Dense) {
+            }
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if constexpr (M == Mode::Dense) {
+                if (lane == 0) {
+                    for (int j = 0; ok && j < it.nbk; ++j) {
+                        const int gj = g + j, st = gj & 1;
+                        const uint32_t ph = (gj >> 1) & 1;
+                        if (!(ok = mbar_wait(bar(K_EMPTY + st), ph ^ 1, abort_flag, 1))) break;
+                        mbar_arrive_expect_tx(bar(K_FULL + st), kLoadBytes);
 #pragma unroll
                         for (int hf = 0; hf < HD / 64; ++hf)
-                            tma_load_3d(dst + hf * kHalfBytes, map, full, hf * 64, j * BN, it.kvh);
-                    } else {
+                            tma_load_3d(sbase + OFF_K + st * kTileBytes + hf * kHalfBytes, &tmk,
+                                        bar(K_FULL + st), hf * 64, j * BN, it.kvh);
+                        if (!(ok = mbar_wait(bar(V_EMPTY + st), ph ^ 1, abort_flag, 2))) break;
+                        mbar_arrive_expect_tx(bar(V_FULL + st), kLoadBytes);
 #pragma unroll
-                        for (int pg = 0; pg < 8; ++pg) {
-                            const int pi = it.p_begin + j * 8 + pg;
-                            int row = p.num_pages * p.Hkv;           // out of range: zeros
-                            if (pi < it.p_end) {
-                                const int page = ids[pg];
-                                if (static_cast<unsigned>(page) >= static_cast<unsigned>(p.num_pages))
-                                    atomicCAS(&g_device_error, 0, 201);
-                                else
-                                    row = page * p.Hkv + kv_head;
-                            }
-#pragma unroll
-                            for (int hf = 0; hf < HD / 64; ++hf)
-                                tma_load_3d(dst + hf * kHalfBytes + pg * kPageBoxBytes, map, full,
-                                            hf * 64, 0, row);
-                        }
+                        for (int hf = 0; hf < HD / 64; ++hf)
+                            tma_load_3d(sbase + OFF_V + st * kTileBytes + hf * kHalfBytes, &tmv,
+                                        bar(V_FULL + st), hf * 64, j * BN, it.kvh);
                     }
+                }
+            } else if (ok) {
+                // Pages: a 128-key tile is 8 pages x (HD / 64) boxes of [16 rows][64 dims].
+                // Lane 2 * page + half issues one box of K and one of V, so the whole tile's
+                // boxes go out at once; its page id is fetched one block ahead.  Lane 0 waits
+                // for the free stage and posts the tile's byte count before the boxes are
+                // issued (the shuffle orders it).
+                const int32_t* bt_row = (M == Mode::Prefix) ? p.bt + (size_t)it.src * p.max_pages
+                                                            : p.bt + (size_t)it.sess * p.max_pages;
+                const int kv_head = (M == Mode::Paged) ? it.kvh : it.h;
+                const int pg = lane >> 1, hf = lane & 1;
+                const bool loader = lane < 16 && hf < HD / 64;
+                auto page_row = [&](int j) -> int {
+                    const int pi = it.p_begin + j * 8 + pg;
+                    int row = p.num_pages * p.Hkv;                   // out of range: zeros
+                    if (loader && pi < it.p_end) {
+                        const int page = __ldg(bt_row + pi);
+                        if (static_cast<unsigned>(page) >= static_cast<unsigned>(p.num_pages))
+                            atomicCAS(&g_device_error, 0, 201);
+                        else
+                            row = page * p.Hkv + kv_head;
+                    }
+                    return row;
                 };
-                if constexpr (M != Mode::Dense) fetch_ids(0);
-                for (int j = 0; ok && j < it.nbk; ++j) {
+                int row = page_row(0);
+                const uint32_t box = hf * kHalfBytes + pg * kPageBoxBytes;
+                for (int j = 0; j < it.nbk; ++j) {
                     const int gj = g + j, st = gj & 1;
                     const uint32_t ph = (gj >> 1) & 1;
-                    if (!(ok = mbar_wait(bar(K_EMPTY + st), ph ^ 1, abort_flag, 1))) break;
-                    mbar_arrive_expect_tx(bar(K_FULL + st), kLoadBytes);
-                    load_kv(&tmk, sbase + OFF_K + st * kTileBytes, bar(K_FULL + st), j);
-                    if (!(ok = mbar_wait(bar(V_EMPTY + st), ph ^ 1, abort_flag, 2))) break;
-                    mbar_arrive_expect_tx(bar(V_FULL + st), kLoadBytes);
-                    load_kv(&tmv, sbase + OFF_V + st * kTileBytes, bar(V_FULL + st), j);
-                    if constexpr (M != Mode::Dense)
-                        if (j + 1 < it.nbk) fetch_ids(j + 1);
+                    if (lane == 0) {
+                        ok = mbar_wait(bar(K_EMPTY + st), ph ^ 1, abort_flag, 1);
+                        if (ok) mbar_arrive_expect_tx(bar(K_FULL + st), kLoadBytes);
+                    }
+                    if (!(ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0)) break;
+                    if (loader)
+                        tma_load_3d(sbase + OFF_K + st * kTileBytes + box, &tmk, bar(K_FULL + st),
+                                    hf * 64, 0, row);
+                    if (lane == 0) {
+                        ok = mbar_wait(bar(V_EMPTY + st), ph ^ 1, abort_flag, 2);
+                        if (ok) mbar_arrive_expect_tx(bar(V_FULL + st), kLoadBytes);
+                    }
+                    if (!(ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0)) break;
+                    if (loader)
+                        tma_load_3d(sbase + OFF_V + st * kTileBytes + box, &tmv, bar(V_FULL + st),
+                                    hf * 64, 0, row);
+                    if (j + 1 < it.nbk) row = page_row(j + 1);
                 }
             }
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;

@@ -3,6 +3,9 @@
     python -m loopfuse_b200.profile_cases decode  [--sessions 32] [--reps 3]
     python -m loopfuse_b200.profile_cases prefill [--batch 2] [--seq 4096] [--reps 3]
     python -m loopfuse_b200.profile_cases pool
+    python -m loopfuse_b200.profile_cases paged [--sessions 128] [--reps 3]
+    python -m loopfuse_b200.profile_cases epilogue [--tokens 16384] [--reps 3]
+    python -m loopfuse_b200.profile_cases dedup [--sessions 512] [--reps 3]
 
 Each case builds its inputs, runs one warm-up launch and then ``--reps`` launches of the op,
 so a capture can skip the warm-up (``-s``) and take one to three launches (``-c``).  The decode
@@ -61,13 +64,87 @@ def run_pool(reps: int) -> None:
     print("pool fork/append/free x", 1 + reps)
 
 
+def run_paged(sessions: int, reps: int) -> None:
+    """Agent-shaped paged prefill: tool outputs (geometric, mean 120, cap 1024) appended after
+    a 4096-token shared prefix, Llama-3-8B attention shapes, one layer of pages."""
+    import numpy as np
+    from .runtime.kv_pool import KVPool
+    rng = np.random.default_rng(0)
+    lens = [int(x) for x in np.minimum(rng.geometric(1 / 120, size=sessions), 1024)]
+    pool = KVPool(num_layers=1, num_heads=32, num_kv_heads=8, head_dim=128, max_seq_len=8192,
+                  max_slots=sessions + 1, dtype=torch.bfloat16,
+                  num_pages=256 + sum((n + 15) // 16 for n in lens) + 16)
+    root = pool.alloc()
+    kk = torch.randn(4096, 8, 128, device="cuda").bfloat16()
+    pool.write_layer([root], pool.reserve([root], [4096]), 0, kk, kk, [4096])
+    ss = pool.fork(root, 4096, n=sessions)
+    T = sum(lens)
+    kn = torch.randn(T, 8, 128, device="cuda").bfloat16()
+    pool.write_layer(ss, pool.reserve(ss, lens), 0, kn, kn, lens)
+    q = torch.randn(T, 32, 128, device="cuda").bfloat16()
+    table, sl = pool.block_table(ss)
+    cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32, device="cuda")
+    kp, vp = pool.layer_pages(0)
+    for _ in range(1 + reps):
+        att.prefill_paged(q, kp, vp, table, cu, sl, max(lens))
+    torch.cuda.synchronize()
+    fl = sum(4 * 128 * 32 * n * 4096 + 4 * 128 * 32 * n * (n + 1) // 2 for n in lens)
+    print(f"paged prefill sessions={sessions} new_tokens={T} flops={fl:.4e}")
+
+
+def run_epilogue(tokens: int, reps: int) -> None:
+    """Decoder epilogues at Llama-3-8B shapes: fused QKV split + RoPE + page scatter, residual
+    add + RMSNorm, SwiGLU gate."""
+    from . import model_ops as mo
+    from .runtime.kv_pool import KVPool
+    n_sess = 16
+    per = tokens // n_sess
+    pool = KVPool(num_layers=1, num_heads=32, num_kv_heads=8, head_dim=128,
+                  max_seq_len=per + 16, max_slots=n_sess, dtype=torch.bfloat16)
+    ss = [pool.alloc() for _ in range(n_sess)]
+    start = pool.reserve(ss, [per] * n_sess)
+    qkv = torch.randn(per * n_sess, 48 * 128, device="cuda").bfloat16()
+    q = torch.empty(per * n_sess, 32, 128, dtype=torch.bfloat16, device="cuda")
+    inv = 1.0 / (500000.0 ** (torch.arange(0, 128, 2, device="cuda").float() / 128))
+    ang = torch.arange(per + 16, device="cuda").float()[:, None] * inv[None, :]
+    rope = (ang.cos().contiguous(), ang.sin().contiguous())
+    x = torch.randn(per * n_sess, 4096, device="cuda").bfloat16()
+    d = torch.randn_like(x)
+    w = torch.ones(4096, dtype=torch.bfloat16, device="cuda")
+    gu = torch.randn(per * n_sess, 2 * 14336, device="cuda").bfloat16()
+    for _ in range(1 + reps):
+        pool.write_qkv(ss, start, 0, qkv, q, [per] * n_sess, rope=rope)
+        mo.add_rmsnorm(x, d, w, 1e-5)
+        mo.swiglu(gu)
+    torch.cuda.synchronize()
+    print(f"epilogue tokens={per * n_sess}")
+
+
+def run_dedup(sessions: int, reps: int) -> None:
+    """Register one 4096-token prompt, then dedup ``sessions`` requests sharing it."""
+    from .runtime.kv_pool import KVPool
+    pool = KVPool(num_layers=1, num_heads=8, num_kv_heads=8, head_dim=64, max_seq_len=4096,
+                  max_slots=sessions + 1, dtype=torch.bfloat16, num_pages=512)
+    root = pool.alloc()
+    pool.reserve([root], [4096])
+    prompt = torch.randint(0, 128000, (4096,), dtype=torch.int32).tolist()
+    pool.register_prefix(root, prompt)
+    ss = [pool.alloc() for _ in range(sessions)]
+    for _ in range(1 + reps):
+        pool.dedup_prefix(ss, [prompt] * sessions)
+        pool.free(ss)
+    torch.cuda.synchronize()
+    print(f"dedup sessions={sessions} pages={4096 // 16}")
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["decode", "prefill", "pool"])
+    ap.add_argument("case", choices=["decode", "prefill", "pool", "paged", "epilogue", "dedup"])
     ap.add_argument("--sessions", type=int, default=32)
     ap.add_argument("--batch", type=int, default=2)
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--pages-per-split", type=int, default=0)
     a = ap.parse_args(argv)
     torch.cuda.set_device(0)
@@ -75,6 +152,12 @@ def main(argv=None) -> None:
         run_decode(a.sessions, a.reps, a.pages_per_split)
     elif a.case == "prefill":
         run_prefill(a.batch, a.seq, a.reps)
+    elif a.case == "paged":
+        run_paged(a.sessions, a.reps)
+    elif a.case == "epilogue":
+        run_epilogue(a.tokens, a.reps)
+    elif a.case == "dedup":
+        run_dedup(a.sessions, a.reps)
     else:
         run_pool(a.reps)
 
