@@ -77,7 +77,7 @@ constexpr float kRescaleThreshold = 8.0f;
 // Which exp2 pairs of each group of 8 run as a polynomial on the FMA pipe (bit i: pair i % 8);
 // the rest use the MUFU unit.  Balances the two pipes.
 #ifndef LF_POLY_MASK
-#define LF_POLY_MASK 0x88
+#define LF_POLY_MASK 0x80
 #endif
 constexpr unsigned kPolyMask = LF_POLY_MASK;
 
@@ -480,13 +480,20 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
 #pragma unroll
                     for (int i = 0; i < BN; ++i) r[i] = (i < lim) ? r[i] : 0xff800000u;   // -inf
                 }
+                // row max: eight chains of three-input max over the 128 columns
+                static_assert(BN == 128, "row max unrolled for 128 columns");
+                auto sv = [&](int i) { return __uint_as_float(r[i]); };
                 float mxs[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) mxs[i] = __uint_as_float(r[i]);
+                for (int k = 0; k < 8; ++k) mxs[k] = fmax3(sv(k), sv(k + 8), sv(k + 16));
 #pragma unroll
-                for (int i = 8; i < BN; ++i) mxs[i & 7] = fmaxf(mxs[i & 7], __uint_as_float(r[i]));
-                const float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
-                                       fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
+                for (int i = 24; i < 120; i += 16)
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) mxs[k] = fmax3(mxs[k], sv(i + k), sv(i + 8 + k));
+#pragma unroll
+                for (int k = 0; k < 8; ++k) mxs[k] = fmaxf(mxs[k], sv(120 + k));
+                const float mx = fmax3(fmax3(mxs[0], mxs[1], mxs[2]), fmax3(mxs[3], mxs[4], mxs[5]),
+                                       fmaxf(mxs[6], mxs[7]));
                 const float m_blk = mx * p.c;
                 const float m_new = (m_blk > m_run + kRescaleThreshold) ? m_blk : m_run;
                 const float alpha = (m_new == m_run) ? 1.f : fast_exp2(m_run - m_new);

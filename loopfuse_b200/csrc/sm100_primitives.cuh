@@ -141,6 +141,13 @@ __device__ __forceinline__ float2 exp2_poly2(uint64_t t2) {
                        __int_as_float(__float_as_int(pv.y) + (__float_as_int(yv.y) << 23)));
 }
 
+// max of three floats in one instruction (sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 // ---- tcgen05 ----------------------------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t slot_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot_smem),
