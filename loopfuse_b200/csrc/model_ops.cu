@@ -17,12 +17,9 @@ constexpr int kNormVecs = 4;                       // vectors of 8 per thread: d
 
 __device__ __forceinline__ float lo_f(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float hi_f(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
-__device__ __forceinline__ uint32_t pack2(float a, float b) {
-    return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(a))) |
-           (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(b))) << 16);
-}
-__device__ __forceinline__ float rt(float v) {               // round to bf16 and back
-    return __bfloat162float(__float2bfloat16_rn(v));
+__device__ __forceinline__ uint32_t pack2(float a, float b) {    // one packed conversion
+    const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&v);
 }
 
 // One CTA per row.
@@ -79,24 +76,25 @@ add_rmsnorm_kernel(uint16_t* __restrict__ x, const uint16_t* __restrict__ delta,
             uint4 o;
             uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-                ow[k] = pack2(rt(v[i][2 * k] * r) * lo_f(ww[k]), rt(v[i][2 * k + 1] * r) * hi_f(ww[k]));
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t nrm = pack2(v[i][2 * k] * r, v[i][2 * k + 1] * r);   // bf16(x * r)
+                ow[k] = pack2(lo_f(nrm) * lo_f(ww[k]), hi_f(nrm) * hi_f(ww[k]));
+            }
             *reinterpret_cast<uint4*>(orow + vi * 8) = o;
         }
     }
 }
 
-// out[r][j] = bf16(bf16(silu(g)) * u) with g = gu[r][j], u = gu[r][ffn + j].
-__global__ void swiglu_kernel(const uint16_t* __restrict__ gu, uint16_t* __restrict__ out, long rows,
+// out[r][j] = bf16(bf16(silu(g)) * u) with g = gu[r][j], u = gu[r][ffn + j].  grid.x walks the
+// vectors of a row, grid.y the rows (grid-stride).
+__global__ void swiglu_kernel(const uint16_t* __restrict__ gu, uint16_t* __restrict__ out, int rows,
                               int ffn) {
-    const int vpr = ffn / 8;
-    const long total = rows * vpr;
-    for (long idx = blockIdx.x * (long)blockDim.x + threadIdx.x; idx < total;
-         idx += (long)gridDim.x * blockDim.x) {
-        const long r = idx / vpr;
-        const int c = static_cast<int>(idx % vpr) * 8;
-        const uint4 g = *reinterpret_cast<const uint4*>(gu + r * 2 * ffn + c);
-        const uint4 u = *reinterpret_cast<const uint4*>(gu + r * 2 * ffn + ffn + c);
+    const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+    if (c >= ffn) return;
+    for (int r = blockIdx.y; r < rows; r += gridDim.y) {
+        const uint16_t* grow = gu + (long)r * 2 * ffn;
+        const uint4 g = *reinterpret_cast<const uint4*>(grow + c);
+        const uint4 u = *reinterpret_cast<const uint4*>(grow + ffn + c);
         const uint32_t* gw = reinterpret_cast<const uint32_t*>(&g);
         const uint32_t* uw = reinterpret_cast<const uint32_t*>(&u);
         uint4 o;
@@ -104,10 +102,10 @@ __global__ void swiglu_kernel(const uint16_t* __restrict__ gu, uint16_t* __restr
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             const float g0 = lo_f(gw[k]), g1 = hi_f(gw[k]);
-            const float s0 = rt(g0 / (1.f + expf(-g0))), s1 = rt(g1 / (1.f + expf(-g1)));
-            ow[k] = pack2(s0 * lo_f(uw[k]), s1 * hi_f(uw[k]));
+            const uint32_t sl = pack2(g0 / (1.f + expf(-g0)), g1 / (1.f + expf(-g1)));   // bf16(silu)
+            ow[k] = pack2(lo_f(sl) * lo_f(uw[k]), hi_f(sl) * hi_f(uw[k]));
         }
-        *reinterpret_cast<uint4*>(out + r * ffn + c) = o;
+        *reinterpret_cast<uint4*>(out + (long)r * ffn + c) = o;
     }
 }
 
@@ -134,9 +132,10 @@ extern "C" int lf_swiglu(const lf_bf16* gu, lf_bf16* out, int rows, int ffn, voi
     LF_CHECK_ARG(rows >= 0 && ffn > 0 && ffn % 8 == 0, "swiglu: ffn must be a positive multiple of 8");
     LF_CHECK_ARG(gu && out && aligned16(gu) && aligned16(out), "swiglu: null or unaligned buffer");
     if (rows == 0) { clear_error(); return LF_OK; }
-    const long work = (long)rows * (ffn / 8);
-    long blocks = (work + 255) / 256;
-    if (blocks > 148L * 32) blocks = 148L * 32;
-    model::swiglu_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(gu, out, rows, ffn);
+    const int bx = (ffn / 8 + 255) / 256;
+    int by = (148 * 16 + bx - 1) / bx;
+    if (by > rows) by = rows;
+    if (by > 65535) by = 65535;
+    model::swiglu_kernel<<<dim3(bx, by), 256, 0, (cudaStream_t)stream>>>(gu, out, rows, ffn);
     return launch_status("swiglu");
 }

@@ -23,13 +23,13 @@ __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w 
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-    const uint32_t l = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
-    const uint32_t h = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
-    return l | (h << 16);
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);      // one packed conversion
+    return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-// grid-stride over (token, head, vector) with heads ordered q (Hq), k (Hkv), v (Hkv); a vector
-// is 8 dims of the first half of a head together with the matching 8 dims of the second half.
+// One CTA per token (grid-stride over tokens); its threads walk (head, vector) pairs with heads
+// ordered q (Hq), k (Hkv), v (Hkv).  A vector is 8 dims of the first half of a head together with
+// the matching 8 dims of the second half.  vph = D / 16 vectors per head is a power of two.
 __global__ void qkv_rope_append_kernel(Meta m, const int32_t* __restrict__ seq_ids,
                                        const int32_t* __restrict__ start_pos,
                                        const int32_t* __restrict__ cu_tokens, int n, int total_tokens,
@@ -37,66 +37,69 @@ __global__ void qkv_rope_append_kernel(Meta m, const int32_t* __restrict__ seq_i
                                        const float* __restrict__ rope_cos,
                                        const float* __restrict__ rope_sin, int rope_rows,
                                        uint16_t* __restrict__ q_out, uint16_t* __restrict__ kp,
-                                       uint16_t* __restrict__ vp, int Hq, int Hkv, int D) {
+                                       uint16_t* __restrict__ vp, int Hq, int Hkv, int D,
+                                       int vph_shift) {
     if (status_of(m) != LF_OK) return;
-    const int half = D / 2, vph = half / 8;
+    const int half = D / 2, vph_mask = (1 << vph_shift) - 1;
     const int H = Hq + 2 * Hkv;
-    const long work = (long)total_tokens * H * vph;
-    for (long idx = blockIdx.x * (long)blockDim.x + threadIdx.x; idx < work;
-         idx += (long)gridDim.x * blockDim.x) {
-        const int v = (int)(idx % vph);
-        const int h = (int)((idx / vph) % H);
-        const int t = (int)(idx / ((long)vph * H));
+    const int units = H << vph_shift;
+    for (int t = blockIdx.x; t < total_tokens; t += gridDim.x) {
         int lo = 0, hi = n - 1;                      // session i with cu[i] <= t < cu[i+1]
         while (lo < hi) {
             const int mid = (lo + hi + 1) >> 1;
             if (cu_tokens[mid] <= t) lo = mid; else hi = mid - 1;
         }
         const int pos = start_pos[lo] + (t - cu_tokens[lo]);
-        const uint16_t* src = qkv + (long)t * row_stride + (long)h * D + v * 8;
-        uint4 a = *reinterpret_cast<const uint4*>(src);
-        uint4 b = *reinterpret_cast<const uint4*>(src + half);
-        if (rope_cos != nullptr && h < Hq + Hkv) {
-            if (pos < 0 || pos >= rope_rows) {
-                atomicCAS(m.ctrl + LF_CTRL_STATUS, LF_OK, LF_EINVAL);
-                continue;
-            }
-            const float4* cp = reinterpret_cast<const float4*>(rope_cos + (long)pos * half + v * 8);
-            const float4* sp = reinterpret_cast<const float4*>(rope_sin + (long)pos * half + v * 8);
-            const float4 c0 = __ldg(cp), c1 = __ldg(cp + 1), s0 = __ldg(sp), s1 = __ldg(sp + 1);
-            const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-            const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-            uint32_t* aw = reinterpret_cast<uint32_t*>(&a);
-            uint32_t* bw = reinterpret_cast<uint32_t*>(&b);
+        const int s = seq_ids[lo];
+        const bool pos_ok = rope_cos == nullptr || (pos >= 0 && pos < rope_rows);
+        const uint16_t* src_row = qkv + (long)t * row_stride;
+        for (int u = threadIdx.x; u < units; u += blockDim.x) {
+            const int v = u & vph_mask;
+            const int h = u >> vph_shift;
+            const uint16_t* src = src_row + h * D + v * 8;
+            uint4 a = *reinterpret_cast<const uint4*>(src);
+            uint4 b = *reinterpret_cast<const uint4*>(src + half);
+            if (rope_cos != nullptr && h < Hq + Hkv) {
+                if (!pos_ok) {
+                    atomicCAS(m.ctrl + LF_CTRL_STATUS, LF_OK, LF_EINVAL);
+                    continue;
+                }
+                const float4* cp = reinterpret_cast<const float4*>(rope_cos + (long)pos * half + v * 8);
+                const float4* sp = reinterpret_cast<const float4*>(rope_sin + (long)pos * half + v * 8);
+                const float4 c0 = __ldg(cp), c1 = __ldg(cp + 1), s0 = __ldg(sp), s1 = __ldg(sp + 1);
+                const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+                uint32_t* aw = reinterpret_cast<uint32_t*>(&a);
+                uint32_t* bw = reinterpret_cast<uint32_t*>(&b);
 #pragma unroll
-            for (int w = 0; w < 4; ++w) {
-                const float x1l = bf16_lo(aw[w]), x1h = bf16_hi(aw[w]);
-                const float x2l = bf16_lo(bw[w]), x2h = bf16_hi(bw[w]);
-                const float cl = cs[2 * w], ch = cs[2 * w + 1], sl = sn[2 * w], sh = sn[2 * w + 1];
-                const float o1l = __fsub_rn(__fmul_rn(x1l, cl), __fmul_rn(x2l, sl));
-                const float o1h = __fsub_rn(__fmul_rn(x1h, ch), __fmul_rn(x2h, sh));
-                const float o2l = __fadd_rn(__fmul_rn(x2l, cl), __fmul_rn(x1l, sl));
-                const float o2h = __fadd_rn(__fmul_rn(x2h, ch), __fmul_rn(x1h, sh));
-                aw[w] = pack_bf16(o1l, o1h);
-                bw[w] = pack_bf16(o2l, o2h);
+                for (int w = 0; w < 4; ++w) {
+                    const float x1l = bf16_lo(aw[w]), x1h = bf16_hi(aw[w]);
+                    const float x2l = bf16_lo(bw[w]), x2h = bf16_hi(bw[w]);
+                    const float cl = cs[2 * w], ch = cs[2 * w + 1], sl = sn[2 * w], sh = sn[2 * w + 1];
+                    const float o1l = __fsub_rn(__fmul_rn(x1l, cl), __fmul_rn(x2l, sl));
+                    const float o1h = __fsub_rn(__fmul_rn(x1h, ch), __fmul_rn(x2h, sh));
+                    const float o2l = __fadd_rn(__fmul_rn(x2l, cl), __fmul_rn(x1l, sl));
+                    const float o2h = __fadd_rn(__fmul_rn(x2h, ch), __fmul_rn(x1h, sh));
+                    aw[w] = pack_bf16(o1l, o1h);
+                    bw[w] = pack_bf16(o2l, o2h);
+                }
             }
-        }
-        uint16_t* dst;
-        if (h < Hq) {
-            dst = q_out + ((long)t * Hq + h) * D + v * 8;
-        } else {
-            const bool is_k = h < Hq + Hkv;
-            const int kh = is_k ? h - Hq : h - Hq - Hkv;
-            const int s = seq_ids[lo];
-            const int page = m.bt[(long)s * m.M + pos / LF_PAGE_SIZE];
-            if (static_cast<unsigned>(page) >= static_cast<unsigned>(m.P)) {
-                atomicCAS(m.ctrl + LF_CTRL_STATUS, LF_OK, LF_EINVAL);
-                continue;
+            uint16_t* dst;
+            if (h < Hq) {
+                dst = q_out + ((long)t * Hq + h) * D + v * 8;
+            } else {
+                const bool is_k = h < Hq + Hkv;
+                const int kh = is_k ? h - Hq : h - Hq - Hkv;
+                const int page = m.bt[(long)s * m.M + pos / LF_PAGE_SIZE];
+                if (static_cast<unsigned>(page) >= static_cast<unsigned>(m.P)) {
+                    atomicCAS(m.ctrl + LF_CTRL_STATUS, LF_OK, LF_EINVAL);
+                    continue;
+                }
+                dst = (is_k ? kp : vp) + (((long)page * Hkv + kh) * LF_PAGE_SIZE + pos % LF_PAGE_SIZE) * D + v * 8;
             }
-            dst = (is_k ? kp : vp) + (((long)page * Hkv + kh) * LF_PAGE_SIZE + pos % LF_PAGE_SIZE) * D + v * 8;
+            *reinterpret_cast<uint4*>(dst) = a;
+            *reinterpret_cast<uint4*>(dst + half) = b;
         }
-        *reinterpret_cast<uint4*>(dst) = a;
-        *reinterpret_cast<uint4*>(dst + half) = b;
     }
 }
 
@@ -130,11 +133,16 @@ extern "C" int lf_pool_write_qkv(const lf_pool_meta* m, const int32_t* seq_ids,
         LF_CHECK_ARG(rope_rows > 0 && aligned16(rope_cos) && aligned16(rope_sin),
                      "pool write_qkv: rope table must be 16-byte aligned with rows > 0");
     }
-    const long work = (long)total_tokens * (num_q_heads + 2 * num_kv_heads) * (head_dim / 16);
-    qkv_rope_append_kernel<<<grid_for(work, 256), 256, 0, (cudaStream_t)stream>>>(
+    int vph_shift = 0;
+    while ((1 << vph_shift) < head_dim / 16) ++vph_shift;
+    LF_CHECK_ARG((1 << vph_shift) == head_dim / 16, "pool write_qkv: head_dim / 16 must be a power of two");
+    const int units = (num_q_heads + 2 * num_kv_heads) << vph_shift;
+    const int threads = units < 512 ? ((units + 31) / 32) * 32 : 512;
+    const int blocks = total_tokens < 148 * 32 ? total_tokens : 148 * 32;
+    qkv_rope_append_kernel<<<blocks, threads, 0, (cudaStream_t)stream>>>(
         to_meta(m), seq_ids, start_pos, cu_tokens, n, total_tokens,
         static_cast<const uint16_t*>(qkv), (long)qkv_row_stride, rope_cos, rope_sin, rope_rows,
         static_cast<uint16_t*>(q_out), static_cast<uint16_t*>(k_pages),
-        static_cast<uint16_t*>(v_pages), num_q_heads, num_kv_heads, head_dim);
+        static_cast<uint16_t*>(v_pages), num_q_heads, num_kv_heads, head_dim, vph_shift);
     return launch_status("pool write_qkv");
 }
