@@ -113,6 +113,30 @@ int lf_decode_fwd(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* v_pag
                   int num_pages, int max_pages, int pages_per_split, float scale,
                   void* stream);
 
+/* Head-tensor-parallel decode with the all-gather of the outputs fused into the combine
+ * step (the reference has no multi-GPU path).  This rank holds num_kv_heads of the model's KV
+ * heads and computes num_q_heads query heads (all arguments as in lf_decode_fwd for that
+ * slice); each finished row (n, h) is stored into every one of the n_peers outputs
+ * out_peers[k] ([num_seqs][num_q_heads_total][head_dim] bf16, one per rank, this rank's
+ * included) at head head_offset + h, with peer-memory stores, followed by a system-scope
+ * fence.  out_peers is a DEVICE array of pointers (from lf_ipc_import).  The caller orders
+ * readers after every rank's call (e.g. a collective on the same stream). */
+int lf_decode_fwd_gather(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* v_pages,
+                         const int32_t* block_table, const int32_t* seq_lens,
+                         int num_prefix_pages, lf_bf16* const* out_peers, int n_peers,
+                         int head_offset, int num_q_heads_total, float* lse, void* workspace,
+                         size_t workspace_bytes, int num_seqs, int num_q_heads, int num_kv_heads,
+                         int head_dim, int num_pages, int max_pages, int pages_per_split,
+                         float scale, void* stream);
+
+/* Cross-process sharing of one device buffer within a node (no reference counterpart):
+ * lf_ipc_export writes the 64-byte IPC handle of the allocation holding `ptr` and ptr's
+ * offset inside it; lf_ipc_import opens a handle from another process (peer access enabled
+ * on demand) and returns that allocation's base in this process; lf_ipc_close unmaps it. */
+int lf_ipc_export(const void* ptr, void* handle_out, size_t* offset_out);
+int lf_ipc_import(const void* handle, void** base_out);
+int lf_ipc_close(void* base);
+
 /* Decode without any device allocation.  Same computation as lf_decode_fwd,
  * but the split partials live in a fixed array inside the library
  * (LF_DECODE_NOALLOC_SCRATCH_BYTES on every GPU that loads it, held until

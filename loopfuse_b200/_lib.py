@@ -69,6 +69,11 @@ _SIGS = {
                           _P, _P, _P, c_int, c_int, c_int, _P],
     "lf_add_rmsnorm": [_P, _P, _P, _P, c_int, c_int, c_float, _P],
     "lf_swiglu": [_P, _P, c_int, c_int, _P],
+    "lf_decode_fwd_gather": [_P, _P, _P, _P, _P, c_int, _P, c_int, c_int, c_int, _P, _P, c_size_t,
+                             c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_float, _P],
+    "lf_ipc_export": [_P, _P, POINTER(c_size_t)],
+    "lf_ipc_import": [_P, POINTER(c_void_p)],
+    "lf_ipc_close": [_P],
     "lf_registry_init": [POINTER(PrefixRegistry), _P],
     "lf_prefix_hashes": [_P, c_int, _P, _P],
     "lf_pool_register_prefix": [POINTER(PoolMeta), POINTER(PrefixRegistry), c_int, _P, c_int, _P, _P],

@@ -169,10 +169,20 @@ split_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kp,
 }
 
 // One CTA of D/4 threads per (query head, session): merge the session's used slots.
+// Where combine puts a finished row.  n_peers == 0: o [N][Hq][D] of this call.  n_peers > 0
+// (head-tensor-parallel decode): row (n, hq) of every output peers[k] [N][hq_total][D] at head
+// head0 + hq -- the all-gather of the heads' outputs, done by the kernel that finishes them
+// (peer-memory stores over NVLink).
+struct CombineOut {
+    uint16_t* o;
+    uint16_t* const* peers;
+    int n_peers, head0, hq_total;
+};
+
 template <int D>
 __global__ void __launch_bounds__(D / 4)
 combine_kernel(const float* __restrict__ part_o, const float2* __restrict__ part_ml,
-               const int32_t* __restrict__ seq_lens, uint16_t* __restrict__ o,
+               const int32_t* __restrict__ seq_lens, const CombineOut out,
                float* __restrict__ lse, int Hq, int max_pages, int pages_per_split,
                int first_page, int n_slots, int prefix_slot0, int n_prefix_chunks) {
     const int hq = blockIdx.x, n = blockIdx.y;
@@ -207,7 +217,13 @@ combine_kernel(const float* __restrict__ part_o, const float2* __restrict__ part
     uint2 packed;
     packed.x = pack_bf16x2(acc.x * inv, acc.y * inv);
     packed.y = pack_bf16x2(acc.z * inv, acc.w * inv);
-    *reinterpret_cast<uint2*>(o + row * D + d0) = packed;
+    if (out.n_peers == 0) {
+        *reinterpret_cast<uint2*>(out.o + row * D + d0) = packed;
+    } else {
+        const size_t grow = ((size_t)n * out.hq_total + out.head0 + hq) * D + d0;
+        for (int k = 0; k < out.n_peers; ++k) *reinterpret_cast<uint2*>(out.peers[k] + grow) = packed;
+        __threadfence_system();                      // visible to the peers before the kernel ends
+    }
     if (lse != nullptr && threadIdx.x == 0) lse[row] = l > 0.f ? (M + log2f(l)) * kLn2 : -INFINITY;
 }
 
@@ -288,17 +304,16 @@ extern "C" int lf_decode_set_profile_events(void* ev_begin, void* ev_end) {
     return LF_OK;
 }
 
-extern "C" int lf_decode_fwd(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* v_pages,
-                             const int32_t* block_table, const int32_t* seq_lens,
-                             int num_prefix_pages, lf_bf16* o, float* lse, void* workspace,
-                             size_t workspace_bytes, int num_seqs, int num_q_heads,
-                             int num_kv_heads, int head_dim, int num_pages, int max_pages,
-                             int pages_per_split, float scale, void* stream) {
-    LF_CHECK_ARG(q && k_pages && v_pages && block_table && seq_lens && o && workspace,
+static int decode_impl(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* v_pages,
+                       const int32_t* block_table, const int32_t* seq_lens, int num_prefix_pages,
+                       const decode::CombineOut& out, float* lse, void* workspace,
+                       size_t workspace_bytes, int num_seqs, int num_q_heads, int num_kv_heads,
+                       int head_dim, int num_pages, int max_pages, int pages_per_split,
+                       float scale, void* stream) {
+    LF_CHECK_ARG(q && k_pages && v_pages && block_table && seq_lens && workspace,
                  "decode: null pointer argument");
-    LF_CHECK_ARG(aligned16(q) && aligned16(k_pages) && aligned16(v_pages) && aligned16(o) &&
-                     aligned16(workspace),
-                 "decode: q, pages, o and workspace must be 16-byte aligned");
+    LF_CHECK_ARG(aligned16(q) && aligned16(k_pages) && aligned16(v_pages) && aligned16(workspace),
+                 "decode: q, pages and workspace must be 16-byte aligned");
     LF_CHECK_ARG(head_dim == 128 || head_dim == 64, "decode: head_dim must be 64 or 128 (got %d)",
                  head_dim);
     LF_CHECK_ARG(num_seqs > 0 && num_kv_heads > 0 && num_q_heads % num_kv_heads == 0,
@@ -352,14 +367,46 @@ extern "C" int lf_decode_fwd(const lf_bf16* q, const lf_bf16* k_pages, const lf_
     if (prof) LF_CHECK_CUDA(cudaEventRecord(g_prof_end, st));
     dim3 cgrid(num_q_heads, num_seqs);
     if (head_dim == 128)
-        decode::combine_kernel<128><<<cgrid, 32, 0, st>>>(po, pml, seq_lens, o, lse, num_q_heads,
+        decode::combine_kernel<128><<<cgrid, 32, 0, st>>>(po, pml, seq_lens, out, lse, num_q_heads,
                                                           max_pages, pages_per_split, num_prefix_pages,
                                                           n_slots, max_split, n_prefix_chunks);
     else
-        decode::combine_kernel<64><<<cgrid, 16, 0, st>>>(po, pml, seq_lens, o, lse, num_q_heads,
+        decode::combine_kernel<64><<<cgrid, 16, 0, st>>>(po, pml, seq_lens, out, lse, num_q_heads,
                                                          max_pages, pages_per_split, num_prefix_pages,
                                                          n_slots, max_split, n_prefix_chunks);
     return launch_status("decode combine");
+}
+
+extern "C" int lf_decode_fwd(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* v_pages,
+                             const int32_t* block_table, const int32_t* seq_lens,
+                             int num_prefix_pages, lf_bf16* o, float* lse, void* workspace,
+                             size_t workspace_bytes, int num_seqs, int num_q_heads,
+                             int num_kv_heads, int head_dim, int num_pages, int max_pages,
+                             int pages_per_split, float scale, void* stream) {
+    LF_CHECK_ARG(o != nullptr && aligned16(o), "decode: o must be a 16-byte aligned pointer");
+    const decode::CombineOut out{o, nullptr, 0, 0, num_q_heads};
+    return decode_impl(q, k_pages, v_pages, block_table, seq_lens, num_prefix_pages, out, lse,
+                       workspace, workspace_bytes, num_seqs, num_q_heads, num_kv_heads, head_dim,
+                       num_pages, max_pages, pages_per_split, scale, stream);
+}
+
+extern "C" int lf_decode_fwd_gather(const lf_bf16* q, const lf_bf16* k_pages,
+                                    const lf_bf16* v_pages, const int32_t* block_table,
+                                    const int32_t* seq_lens, int num_prefix_pages,
+                                    lf_bf16* const* out_peers, int n_peers, int head_offset,
+                                    int num_q_heads_total, float* lse, void* workspace,
+                                    size_t workspace_bytes, int num_seqs, int num_q_heads,
+                                    int num_kv_heads, int head_dim, int num_pages, int max_pages,
+                                    int pages_per_split, float scale, void* stream) {
+    LF_CHECK_ARG(out_peers != nullptr && n_peers > 0 && n_peers <= 64,
+                 "decode gather: need 1..64 output pointers (a device array)");
+    LF_CHECK_ARG(head_offset >= 0 && head_offset + num_q_heads <= num_q_heads_total,
+                 "decode gather: heads [%d, %d) outside the %d output heads", head_offset,
+                 head_offset + num_q_heads, num_q_heads_total);
+    const decode::CombineOut out{nullptr, out_peers, n_peers, head_offset, num_q_heads_total};
+    return decode_impl(q, k_pages, v_pages, block_table, seq_lens, num_prefix_pages, out, lse,
+                       workspace, workspace_bytes, num_seqs, num_q_heads, num_kv_heads, head_dim,
+                       num_pages, max_pages, pages_per_split, scale, stream);
 }
 
 // ---- decode without device allocation ------------------------------------------------------
@@ -483,11 +530,15 @@ extern "C" int lf_decode_fwd_noalloc(const lf_bf16* q, const lf_bf16* k_pages,
     }
     dim3 cgrid(num_q_heads, num_seqs);
     if (head_dim == 128)
-        decode::combine_kernel<128><<<cgrid, 32, 0, st>>>(po, pml, seq_lens, o, lse, num_q_heads,
+        decode::combine_kernel<128><<<cgrid, 32, 0, st>>>(po, pml, seq_lens,
+                                                          decode::CombineOut{o, nullptr, 0, 0, num_q_heads},
+                                                          lse, num_q_heads,
                                                           max_pages, pps, num_prefix_pages,
                                                           n_slots, max_split, n_prefix_chunks);
     else
-        decode::combine_kernel<64><<<cgrid, 16, 0, st>>>(po, pml, seq_lens, o, lse, num_q_heads,
+        decode::combine_kernel<64><<<cgrid, 16, 0, st>>>(po, pml, seq_lens,
+                                                         decode::CombineOut{o, nullptr, 0, 0, num_q_heads},
+                                                         lse, num_q_heads,
                                                          max_pages, pps, num_prefix_pages,
                                                          n_slots, max_split, n_prefix_chunks);
     return launch_status("decode noalloc combine");
