@@ -63,6 +63,7 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-fusion", action="store_true")
     ap.add_argument("--no-agent", action="store_true", help="skip the agent-loop sub-object")
+    ap.add_argument("--no-head-tp", action="store_true", help="skip the head-parallel decode (N>1)")
     ap.add_argument("--workload", choices=["decode", "agent"], default="decode")
     ap.add_argument("--agent-sessions", type=int, default=512)
     ap.add_argument("--agent-steps", type=int, default=10)
@@ -469,6 +470,52 @@ def main():
         del loop
         torch.cuda.empty_cache()
 
+    # ---------------- head-tensor-parallel decode (N > 1): same sessions on every rank, ------
+    # each rank holding Hkv / N KV heads; outputs of all heads gathered on every rank ----------
+    head_tp = None
+    if world > 1 and not args.no_head_tp and 8 % world == 0:
+        torch.cuda.empty_cache()
+        from loopfuse_b200.runtime.head_tp import HeadParallelDecode
+        wt = decode_inputs(N=args.sessions, Hq=32 // world, Hkv=8 // world,
+                           seed=args.seed + 5000, device=dev)
+        tN, thq, tD = wt.q.shape
+        tmax = wt.block_table.shape[1]
+        tpps = att.default_pages_per_split(tN, wt.k_pages.shape[1], tmax)
+        tws = torch.empty(att.decode_workspace_bytes(tN, thq, tD, tmax, tpps, wt.n_prefix_pages),
+                          dtype=torch.uint8, device=dev)
+        tp = HeadParallelDecode(tN, 32, tD, dev)
+        args_tp = (wt.q, wt.k_pages, wt.v_pages, wt.block_table, wt.seq_lens)
+        kw_tp = dict(num_prefix_pages=wt.n_prefix_pages, pages_per_split=tpps, workspace=tws)
+        timings = {}
+        for name, fn in (("fused", tp.decode), ("nccl", tp.decode_nccl)):
+            for _ in range(W):
+                fn(*args_tp, **kw_tp)
+            torch.cuda.synchronize()
+            barrier()
+            a_ev, b_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a_ev.record(stream)
+            for _ in range(K):
+                fn(*args_tp, **kw_tp)
+            b_ev.record(stream)
+            torch.cuda.synchronize()
+            barrier()
+            timings[name] = max_over_ranks(a_ev.elapsed_time(b_ev) / K)
+        tb = world * decode_bytes(wt)["unique"]
+        head_tp = {"workload": f"paged decode, {tN} sessions on every rank, KV heads split {world} ways "
+                               f"({8 // world} KV / {thq} query heads per rank), outputs of all 32 heads "
+                               f"gathered on every rank",
+                   "fused_gather": {"ms_per_step": round(timings["fused"], 4),
+                                    "GBps": round(tb / (timings["fused"] * 1e-3) / 1e9, 1),
+                                    "how": "combine kernel stores into every rank's output over IPC-mapped "
+                                           "peer memory; one 4-byte NCCL all-reduce orders readers"},
+                   "nccl_all_gather": {"ms_per_step": round(timings["nccl"], 4),
+                                       "GBps": round(tb / (timings["nccl"] * 1e-3) / 1e9, 1),
+                                       "how": "local decode, all_gather_into_tensor, head-major re-layout"},
+                   "bytes_per_step": tb}
+        tp.close()
+        del wt, tws, tp, args_tp, kw_tp
+        torch.cuda.empty_cache()
+
     # ---------------- agent loop (512 sessions x 10 ReAct steps, Llama-3-8B shapes) ----------
     agent = None
     if not args.no_agent:
@@ -515,6 +562,7 @@ def main():
             "prefill": prefill,
             "kv_fusion_loop": fusion,
             "agent_loop": agent,
+            "head_tp": head_tp,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
