@@ -331,6 +331,13 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    def sum_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
     peaks = load_peaks()
     K, W = args.steps, max(3, args.warmup)
 
@@ -382,7 +389,8 @@ def main():
     launches_per_step = 3 if w.n_prefix_pages else 2
     n_prefix = w.n_prefix_pages
     pool_gb = round(2 * w.k_pages.numel() * w.k_pages.element_size() / 1e9, 2)
-    value = world * nb["unique"] / (ms * 1e-3) / 1e9
+    job_bytes = sum_over_ranks(float(nb["unique"]))      # every rank's own sessions
+    value = job_bytes / (ms * 1e-3) / 1e9
 
     # ---------------- end to end through the public API, host buffers ----------------
     q_h = w.q.cpu().pin_memory()
@@ -543,6 +551,7 @@ def main():
                        "kv_heads": Hkv, "head_dim": D, "pages_per_split": pps,
                        "prefix_pages": n_prefix, "pool_gb_per_gpu": pool_gb,
                        "unique_bytes_per_step": nb["unique"], "logical_bytes_per_step": nb["logical"],
+                       "job_unique_bytes_per_step": int(job_bytes),
                        "l2": "inputs larger than L2 (K/V pool ~17 GB per GPU); no flush",
                        "parallelism": f"session-sharded x{world}, no collective in the timed region"},
             "roofline": {"bound": "hbm", "kernel": "decode split (per-session pages)",
@@ -554,7 +563,7 @@ def main():
                          "op_frac": round(value / world / peaks["hbm_gbs"], 4),
                          "peak_source": peaks["source"]},
             "cpu_baseline": cpu,
-            "e2e": {"value": round(world * nb["unique"] / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "e2e": {"value": round(job_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": launches_per_step * K,
