@@ -9,7 +9,9 @@ exponentially distributed latency (mean ``tool_ms``) while the GPU serves other 
 
 Scheduling (one host thread per GPU, a loop of GPU batches):
   1. sessions whose tool has returned move to "prefill";
-  2. if any session waits for prefill, one varlen prefill batch of all of them (capped at
+  2. if sessions wait for prefill -- and, while others are decoding, either at least
+     ``min_prefill_tokens`` tokens are pending or the oldest request has waited
+     ``max_prefill_wait_ms`` -- one varlen prefill batch of them (capped at
      ``max_prefill_tokens``) runs and yields each session's first decoded token;
   3. otherwise one decode iteration advances every decoding session by one token; sessions
      that finish their thought/action start their tool call;
@@ -57,6 +59,11 @@ class AgentLoopConfig:
     speculative: bool = True
     graphs: bool = True              # decode iterations replayed from CUDA graphs
     max_prefill_tokens: int = 16384
+    # While sessions are decoding, a prefill batch waits until this many tokens are pending or
+    # its oldest request has waited max_prefill_wait_ms: each forward reads all the weights, so
+    # tiny prefill batches (a few returning tools at a time) cost a whole forward each.
+    min_prefill_tokens: int = 2048
+    max_prefill_wait_ms: float = 25.0
     seed: int = 0
 
 
@@ -72,6 +79,7 @@ class _Sess:
     last_token: int = 0
     spec_done: bool = False
     ready_at: float = 0.0
+    pending_since: float = 0.0
 
 
 @dataclass
@@ -167,6 +175,7 @@ class AgentLoop:
         sessions = [_Sess(i, st, k) for k, (i, st) in enumerate(zip(self.ids, states))]
         for s in sessions:
             s.pending = [int(x) for x in self.rng.integers(0, self.vocab, size=cfg.question_tokens)]
+            s.pending_since = t_start
         tools: List = []                            # heap of (ready_at, idx in sessions)
         while True:
             now = time.perf_counter()
@@ -177,8 +186,14 @@ class AgentLoop:
                 obs = [] if s.spec_done else list(self.template)
                 s.pending = obs + [int(x) for x in self.rng.integers(0, self.vocab, size=out_len)]
                 s.phase = "prefill"
+                s.pending_since = now
             pre = [s for s in sessions if s.phase == "prefill"]
             dec = [s for s in sessions if s.phase == "decode"]
+            if pre and dec:
+                waited_ms = (now - min(s.pending_since for s in pre)) * 1000.0
+                if (sum(len(s.pending) for s in pre) < cfg.min_prefill_tokens
+                        and waited_ms < cfg.max_prefill_wait_ms):
+                    pre = []                        # let more requests gather; decode meanwhile
             if pre:
                 batch, budget = [], cfg.max_prefill_tokens
                 for s in pre:
