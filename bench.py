@@ -445,6 +445,13 @@ def main():
         torch.cuda.synchronize()
         barrier()
         p_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in pev) / K)
+        # clocks under prefill load: an untimed window of the same launches (~0.6 s), sampled
+        # by nvidia-smi, right after the timed ones
+        with ClockSampler(uuid) as pclk:
+            for _ in range(max(1, int(600.0 / max(p_ms, 1e-3)))):
+                att.prefill_attention_fwd(pq, pk, pv, causal=True)
+            torch.cuda.synchronize()
+        prefill_clocks = pclk.summary()
         tflops = flops / (p_ms * 1e-3) / 1e12
         prefill = {"metric": "prefill TFLOP/s", "workload": PREFILL_WORKLOAD,
                    "value": round(world * tflops, 2), "unit": "TFLOP/s", "ms_per_step": round(p_ms, 4),
@@ -453,7 +460,8 @@ def main():
                                 "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                                 "frac": round(tflops / peaks["bf16_tflops"], 4),
                                 "traffic": profile_traffic("prefill_causal_b8_s4096.txt"),
-                                "peak_source": peaks["source"] + " (burst)"}}
+                                "peak_source": peaks["source"] + " (burst)"},
+                   "clocks_under_load": prefill_clocks}
 
     # ---------------- KV-fusion loop (64 sessions x 8 steps, Llama-3-8B attention shapes) ----
     fusion = None

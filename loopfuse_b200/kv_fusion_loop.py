@@ -15,6 +15,9 @@ by the paged split-KV decode with the shared prefix, in every one of ``layers`` 
 Attention shapes are Llama-3-8B's (32 layers, 32 query / 8 KV heads, head_dim 128, bf16);
 the K/V/q values are synthetic (no model weights are involved).
 
+After the first decode iteration, every decode iteration (all sessions, one token, every layer)
+is replayed from one CUDA graph: the session set is fixed, so its shapes are.
+
 Per step it reports the algorithmic HBM bytes the attention reads with prefix sharing
 (``bytes_read``: every page a kernel must touch, the prefix once per decode call) and without
 it (``bytes_read_unshared``: the prefix once per session), the K/V bytes written, and the GPU
@@ -49,6 +52,7 @@ class FusionLoopConfig:
     tool_mean: float = 120.0
     tool_cap: int = 1024
     seed: int = 0
+    graphs: bool = True          # decode iterations after the first replayed from a CUDA graph
 
 
 def tool_lengths(cfg: FusionLoopConfig) -> np.ndarray:
@@ -104,6 +108,10 @@ class FusionLoop:
         self.qdec = rnd(c.sessions, c.q_heads, c.head_dim)
         self.page_bytes = 2 * c.kv_heads * PAGE * c.head_dim * 2       # K+V of one page, one layer
         self.checks = 0
+        self._graph: Optional[dict] = None
+        self._dec_idx = None
+        self._ws: Optional[torch.Tensor] = None
+        self._pps = 0
 
     # -- oracle mirror ----------------------------------------------------------------------
     def _check(self):
@@ -164,25 +172,36 @@ class FusionLoop:
             self._check()
         # decode: one token per session per iteration, every layer
         ones = [1] * len(S)
-        dec_idx = pool.batch_index(S, ones)
-        ws = None
+        if self._dec_idx is None:
+            self._dec_idx = pool.batch_index(S, ones)
+        dec_idx = self._dec_idx
         for _ in range(c.decode_tokens):
-            start = pool.reserve(S, ones)
-            table, lens = pool.block_table(S)
-            for layer in range(c.layers):
-                pool.write_layer(S, start, layer, self.kbuf[:len(S)], self.vbuf[:len(S)], ones,
-                                 index=dec_idx)
-                kp, vp = pool.layer_pages(layer)
-                if ws is None:
-                    pps = att.default_pages_per_split(len(S), c.kv_heads, table.shape[1])
-                    ws = torch.empty(att.decode_workspace_bytes(len(S), c.q_heads, c.head_dim,
-                                                                table.shape[1], pps,
-                                                                self.n_prefix_pages),
-                                     dtype=torch.uint8, device=self.device)
-                att.paged_decode(self.qdec[:len(S)], kp, vp, table, lens,
-                                 num_prefix_pages=self.n_prefix_pages, pages_per_split=pps,
-                                 workspace=ws)
-                launches += 4
+            if self._graph is not None:
+                for s in S:
+                    if s.current_len + 1 > pool.max_seq_len:
+                        raise RuntimeError(f"KV cache overflow: current_len={s.current_len} + "
+                                           f"seq_new=1 > max_seq_len={pool.max_seq_len}")
+                self._graph["graph"].replay()
+                for s in S:
+                    s.current_len += 1
+            else:
+                start = pool.reserve(S, ones)
+                table, lens = pool.block_table(S)
+                for layer in range(c.layers):
+                    pool.write_layer(S, start, layer, self.kbuf[:len(S)], self.vbuf[:len(S)], ones,
+                                     index=dec_idx)
+                    kp, vp = pool.layer_pages(layer)
+                    if self._ws is None:
+                        self._pps = att.default_pages_per_split(len(S), c.kv_heads, table.shape[1])
+                        self._ws = torch.empty(att.decode_workspace_bytes(
+                            len(S), c.q_heads, c.head_dim, table.shape[1], self._pps,
+                            self.n_prefix_pages), dtype=torch.uint8, device=self.device)
+                    att.paged_decode(self.qdec[:len(S)], kp, vp, table, lens,
+                                     num_prefix_pages=self.n_prefix_pages,
+                                     pages_per_split=self._pps, workspace=self._ws)
+                if c.graphs:
+                    self._graph = self._capture_decode(S, dec_idx)
+            launches += 2 + 4 * c.layers
             own = sum(self._pages(s.current_len) - self.n_prefix_pages for s in S)
             bytes_read += c.layers * (self.n_prefix_pages + own) * self.page_bytes
             bytes_unshared += c.layers * sum(self._pages(s.current_len) for s in S) * self.page_bytes
@@ -191,9 +210,34 @@ class FusionLoop:
                 self._check()
         ev1.record()
         ev1.synchronize()
+        if pool.status() != 0:
+            pool._raise_if_failed("fusion-loop decode")
         written = c.layers * (total + c.decode_tokens * len(S)) * 2 * c.kv_heads * c.head_dim * 2
         return StepStats(step, total, ev0.elapsed_time(ev1), bytes_read, bytes_unshared, written,
                          launches)
+
+    def _capture_decode(self, S, dec_idx) -> dict:
+        """One decode iteration of every session as a CUDA graph: pool reserve and block-table
+        gather on device buffers, then per layer the K/V append and the paged decode.  Captured
+        after an eager iteration has initialised every kernel; nothing in it allocates."""
+        c, pool, n = self.cfg, self.pool, len(S)
+        i32 = dict(dtype=torch.int32, device=self.device)
+        g = {"start": torch.empty(n, **i32), "ones": torch.ones(n, **i32),
+             "table": torch.empty((n, pool.max_pages_per_seq), **i32), "lens": torch.empty(n, **i32),
+             "out": torch.empty_like(self.qdec[:n])}
+        kb, vb, qd = self.kbuf[:n], self.vbuf[:n], self.qdec[:n]
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            pool.reserve_device(dec_idx[0], g["ones"], g["start"], n)
+            pool.gather_device(dec_idx[0], n, g["table"], g["lens"])
+            for layer in range(c.layers):
+                pool.write_layer(S, g["start"], layer, kb, vb, [1] * n, index=dec_idx)
+                kp, vp = pool.layer_pages(layer)
+                att.paged_decode(qd, kp, vp, g["table"], g["lens"],
+                                 num_prefix_pages=self.n_prefix_pages, pages_per_split=self._pps,
+                                 out=g["out"], workspace=self._ws)
+        g["graph"] = graph
+        return g
 
     def teardown(self):
         everyone = self.sessions + [self.root]

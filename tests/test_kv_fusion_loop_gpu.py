@@ -39,3 +39,21 @@ def test_decode_in_the_loop_matches_oracle():
     d = (o.float().cpu() - ref).abs()
     assert d.max().item() <= 2e-2 and d.mean().item() <= 2e-3
     loop.teardown()
+
+
+def test_graphed_decode_iterations_equal_eager():
+    """Graph replays of the decode iteration leave the pool exactly as eager iterations do."""
+    res = []
+    for graphs in (False, True):
+        cfg = FusionLoopConfig(sessions=7, steps=2, layers=3, prefix_tokens=96, decode_tokens=5,
+                               tool_mean=25, tool_cap=60, seed=11, graphs=graphs)
+        loop = FusionLoop(cfg)
+        loop.setup()
+        for st in range(cfg.steps):
+            loop.step(st)
+        torch.cuda.synchronize()
+        res.append((loop.pool.snapshot(), loop.pool.keys.clone(), loop.pool.values.clone(),
+                    [s.current_len for s in loop.sessions]))
+    (se, ke, ve, le), (sg, kg, vg, lg) = res
+    assert le == lg and se == sg
+    assert torch.equal(ke, kg) and torch.equal(ve, vg)
