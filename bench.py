@@ -347,7 +347,7 @@ def main():
     N, Hq, D = w.q.shape
     Hkv = w.k_pages.shape[1]
     max_pages = w.block_table.shape[1]
-    pps = args.pages_per_split or att.default_pages_per_split(N, Hkv, max_pages)
+    pps = args.pages_per_split or att.default_pages_per_split(N, Hkv, max_pages, w.n_prefix_pages)
     ws = torch.empty(att.decode_workspace_bytes(N, Hq, D, max_pages, pps, w.n_prefix_pages),
                      dtype=torch.uint8, device=dev)
     out = torch.empty_like(w.q)
@@ -496,7 +496,7 @@ def main():
                            seed=args.seed + 5000, device=dev)
         tN, thq, tD = wt.q.shape
         tmax = wt.block_table.shape[1]
-        tpps = att.default_pages_per_split(tN, wt.k_pages.shape[1], tmax)
+        tpps = att.default_pages_per_split(tN, wt.k_pages.shape[1], tmax, wt.n_prefix_pages)
         tws = torch.empty(att.decode_workspace_bytes(tN, thq, tD, tmax, tpps, wt.n_prefix_pages),
                           dtype=torch.uint8, device=dev)
         tp = HeadParallelDecode(tN, 32, tD, dev)

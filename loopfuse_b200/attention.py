@@ -91,10 +91,14 @@ def prefill_paged(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torch.Tensor,
     return (o, lse) if return_lse else o
 
 
-def default_pages_per_split(num_seqs: int, num_kv_heads: int, max_pages: int) -> int:
-    """Split size: enough CTAs for several waves on 148 SMs, at most 128 pages each."""
+def default_pages_per_split(num_seqs: int, num_kv_heads: int, max_pages: int,
+                            num_prefix_pages: int = 0) -> int:
+    """Split size for the sessions' own pages (the shared prefix is read separately): enough
+    CTAs for several waves on 148 SMs, 8 to 128 pages each.  ``max_pages`` is the block-table
+    width, each session's capacity; sessions are taken to be half full on average."""
     target_ctas = SM_COUNT * 3 * 8
-    per = max(1, (num_seqs * num_kv_heads * max_pages) // target_ctas)
+    own = max(1, (max_pages - num_prefix_pages) // 2)
+    per = max(1, (num_seqs * num_kv_heads * own) // target_ctas)
     pps = 8
     while pps < per and pps < 128:
         pps *= 2
@@ -133,7 +137,7 @@ def paged_decode(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torch.Tensor,
     if block_table.dim() != 2 or block_table.shape[0] != N or seq_lens.shape != (N,):
         raise LoopfuseError(_lib.LF_EINVAL, "block_table must be [N,max_pages], seq_lens [N]")
     max_pages = block_table.shape[1]
-    pps = pages_per_split or default_pages_per_split(N, Hkv, max_pages)
+    pps = pages_per_split or default_pages_per_split(N, Hkv, max_pages, num_prefix_pages)
     scale = D ** -0.5 if scale is None else float(scale)
     need = decode_workspace_bytes(N, Hq, D, max_pages, pps, num_prefix_pages)
     if workspace is None or workspace.numel() * workspace.element_size() < need:

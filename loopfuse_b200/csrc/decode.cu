@@ -258,7 +258,9 @@ inline int suffix_splits(int max_pages, int pps, int n_prefix) {
 }
 // Shared-prefix pages are cut into chunks of at most 32 pages (one tensor-core CTA each) so the
 // prefix pass fills the GPU even when sessions use long splits.
-inline int prefix_chunk_pages(int pps) { return pps < 32 ? pps : 32; }
+// Shared-prefix chunk: 16..32 pages (a small split size must not shred the prefix into many
+// partials for the combine step).
+inline int prefix_chunk_pages(int pps) { return pps < 16 ? 16 : (pps < 32 ? pps : 32); }
 inline int prefix_chunks(int pps, int n_prefix) {
     const int c = prefix_chunk_pages(pps);
     return (n_prefix + c - 1) / c;

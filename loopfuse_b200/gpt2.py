@@ -103,7 +103,7 @@ class GPT2Model:
                          for s0, n in zip(starts_host, counts)])
         decode = all(n == 1 for n in counts)
         if decode:
-            pps = att.default_pages_per_split(len(states), c.heads, table.shape[1])
+            pps = att.default_pages_per_split(len(states), c.heads, table.shape[1], n_prefix_pages)
             need = att.decode_workspace_bytes(len(states), c.heads, c.head_dim, table.shape[1],
                                               pps, n_prefix_pages)
             if self._ws is None or self._ws.numel() < need:

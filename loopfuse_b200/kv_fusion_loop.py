@@ -192,7 +192,8 @@ class FusionLoop:
                                      index=dec_idx)
                     kp, vp = pool.layer_pages(layer)
                     if self._ws is None:
-                        self._pps = att.default_pages_per_split(len(S), c.kv_heads, table.shape[1])
+                        self._pps = att.default_pages_per_split(len(S), c.kv_heads, table.shape[1],
+                                                                self.n_prefix_pages)
                         self._ws = torch.empty(att.decode_workspace_bytes(
                             len(S), c.q_heads, c.head_dim, table.shape[1], self._pps,
                             self.n_prefix_pages), dtype=torch.uint8, device=self.device)

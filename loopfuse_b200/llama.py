@@ -159,7 +159,7 @@ class LlamaShaped:
             cu = torch.tensor([0] + list(torch.tensor(counts).cumsum(0)), dtype=torch.int32,
                               device=self.device)
         else:
-            pps = att.default_pages_per_split(len(states), c.kv_heads, table.shape[1])
+            pps = att.default_pages_per_split(len(states), c.kv_heads, table.shape[1], n_prefix_pages)
             need = att.decode_workspace_bytes(len(states), c.q_heads, c.head_dim, table.shape[1],
                                               pps, n_prefix_pages)
             if self._ws is None or self._ws.numel() < need:
@@ -239,7 +239,7 @@ class GraphedDecode:
              "table": torch.empty((nb, pool.max_pages_per_seq), dtype=torch.int32, device=dev),
              "lens": torch.empty(nb, dtype=torch.int32, device=dev),
              "copied": torch.cuda.Event()}
-        s["pps"] = att.default_pages_per_split(nb, c.kv_heads, pool.max_pages_per_seq)
+        s["pps"] = att.default_pages_per_split(nb, c.kv_heads, pool.max_pages_per_seq, self.npp)
         s["ws"] = torch.empty(att.decode_workspace_bytes(nb, c.q_heads, c.head_dim,
                                                          pool.max_pages_per_seq, s["pps"], self.npp),
                               dtype=torch.uint8, device=dev)

@@ -25,7 +25,7 @@ from .workloads import decode_bytes, decode_inputs, prefill_flops, prefill_input
 def run_decode(sessions: int, reps: int, pps: int) -> None:
     w = decode_inputs(N=sessions, seed=0)
     max_pages = w.block_table.shape[1]
-    pps = pps or att.default_pages_per_split(sessions, w.k_pages.shape[1], max_pages)
+    pps = pps or att.default_pages_per_split(sessions, w.k_pages.shape[1], max_pages, w.n_prefix_pages)
     out = torch.empty_like(w.q)
     ws = torch.empty(att.decode_workspace_bytes(sessions, w.q.shape[1], w.q.shape[2], max_pages, pps,
                                                 w.n_prefix_pages), dtype=torch.uint8, device="cuda")

@@ -81,7 +81,7 @@ class HeadParallelDecode:
         self._check(q, k_pages)
         P, Hkv, _, D = k_pages.shape
         max_pages = block_table.shape[1]
-        pps = pages_per_split or att.default_pages_per_split(self.N, Hkv, max_pages)
+        pps = pages_per_split or att.default_pages_per_split(self.N, Hkv, max_pages, num_prefix_pages)
         need = att.decode_workspace_bytes(self.N, self.hq_local, D, max_pages, pps, num_prefix_pages)
         if workspace is None or workspace.numel() * workspace.element_size() < need:
             workspace = torch.empty(need, dtype=torch.uint8, device=self.device)
