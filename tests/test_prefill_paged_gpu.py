@@ -81,3 +81,35 @@ def test_paged_prefill_equals_dense_prefill_on_contiguous_context():
                                    k[0].permute(1, 0, 2).unsqueeze(0).contiguous(),
                                    v[0].permute(1, 0, 2).unsqueeze(0).contiguous())
     assert torch.equal(o.permute(1, 0, 2), od[0])
+
+
+def test_paged_prefill_sessions_without_new_tokens():
+    """A batch may list sessions that append nothing (cu_seqlens repeats): they get no rows and
+    the other sessions' results are unchanged."""
+    g = torch.Generator(device="cuda").manual_seed(21)
+    hq, hkv, D = 8, 2, 128
+    pool = KVPool(num_layers=1, num_heads=hq, num_kv_heads=hkv, head_dim=D, max_seq_len=1024,
+                  max_slots=4, dtype=torch.bfloat16)
+    ss = [pool.allocate_slot() for _ in range(4)]
+    ctx = _rand(1, 200, hkv, D, g=g)
+    pool.append([ss[1]], [ctx], [ctx])                       # cached context, no new tokens
+    counts = [70, 0, 33, 0]
+    start = pool.reserve(ss, counts)
+    T = sum(counts)
+    nk = _rand(T, hkv, D, g=g)
+    pool.write_layer(ss, start, 0, nk, nk, counts)
+    q = _rand(T, hq, D, g=g)
+    table, lens = pool.block_table(ss)
+    cu = torch.tensor([0, 70, 70, 103, 103], dtype=torch.int32, device="cuda")
+    kp, vp = pool.layer_pages(0)
+    o = att.prefill_paged(q, kp, vp, table, cu, lens, max(counts))
+    off = 0
+    for s, n in zip(ss, counts):
+        if n == 0:
+            continue
+        k, v = pool.read(s, 0)
+        qi = q[off:off + n].permute(1, 0, 2).unsqueeze(0)
+        ref, _ = ora.prefill(qi.cpu(), k.unsqueeze(0).cpu(), v.unsqueeze(0).cpu(), causal=True)
+        d = (o[off:off + n].permute(1, 0, 2).unsqueeze(0).float().cpu() - ref).abs()
+        assert d.max().item() <= TOL_MAX and d.mean().item() <= TOL_MEAN
+        off += n
