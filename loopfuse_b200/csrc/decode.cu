@@ -21,6 +21,8 @@
 
 #include <math.h>
 
+#include <mutex>
+
 namespace lf {
 namespace decode {
 
@@ -306,6 +308,34 @@ extern "C" int lf_decode_set_profile_events(void* ev_begin, void* ev_end) {
     return LF_OK;
 }
 
+// The shared-prefix partial pass is latency-bound (a few tensor-core work items) while the split
+// kernel is bandwidth-bound, and they write disjoint partial slots: the prefix pass runs on a
+// library-owned stream forked from the caller's (event record / wait, the pattern stream capture
+// supports) and joins back before the combine.  One side stream and its two events per device,
+// created on first use; a mutex keeps concurrent callers' fork/join pairs from interleaving.
+namespace {
+struct SideStream {
+    cudaStream_t s = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+};
+std::mutex g_side_mu;
+SideStream g_side[64];
+
+int side_stream(SideStream** out) {                  // caller holds g_side_mu
+    int dev = 0;
+    LF_CHECK_CUDA(cudaGetDevice(&dev));
+    LF_CHECK_ARG(dev >= 0 && dev < 64, "decode: device index %d out of range", dev);
+    SideStream& ss = g_side[dev];
+    if (ss.s == nullptr) {
+        LF_CHECK_CUDA(cudaStreamCreateWithFlags(&ss.s, cudaStreamNonBlocking));
+        LF_CHECK_CUDA(cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming));
+        LF_CHECK_CUDA(cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming));
+    }
+    *out = &ss;
+    return LF_OK;
+}
+}  // namespace
+
 static int decode_impl(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* v_pages,
                        const int32_t* block_table, const int32_t* seq_lens, int num_prefix_pages,
                        const decode::CombineOut& out, float* lse, void* workspace,
@@ -341,12 +371,28 @@ static int decode_impl(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* 
     const float qscale = scale * kLog2e;
     const uint16_t* q16 = q;
 
+    const bool overlap = num_prefix_pages > 0 && max_split > 0;
+    std::unique_lock<std::mutex> side_lock(g_side_mu, std::defer_lock);
+    SideStream* side = nullptr;
     if (num_prefix_pages > 0) {
+        cudaStream_t pst = st;
+        if (overlap) {
+            side_lock.lock();
+            int rc = side_stream(&side);
+            if (rc != LF_OK) return rc;
+            LF_CHECK_CUDA(cudaEventRecord(side->fork, st));
+            LF_CHECK_CUDA(cudaStreamWaitEvent(side->s, side->fork, 0));
+            pst = side->s;
+        }
         int rc = decode::launch_prefix(q16, k_pages, v_pages, block_table, seq_lens, po, pml,
                                        num_seqs, num_q_heads, num_kv_heads, head_dim, num_pages,
                                        max_pages, num_prefix_pages, decode::prefix_chunk_pages(pages_per_split), n_slots, max_split,
-                                       qscale, st);
-        if (rc != LF_OK) return rc;
+                                       qscale, pst);
+        if (overlap) cudaEventRecord(side->join, side->s);
+        if (rc != LF_OK) {
+            if (overlap) cudaStreamWaitEvent(st, side->join, 0);   // keep the fork closed
+            return rc;
+        }
     }
     const bool prof = g_prof_begin != nullptr && g_prof_end != nullptr;
     if (prof) LF_CHECK_CUDA(cudaEventRecord(g_prof_begin, st));
@@ -362,11 +408,14 @@ static int decode_impl(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* 
                                                   seq_lens, po, pml, num_q_heads, num_kv_heads,
                                                   num_pages, max_pages, pages_per_split, num_prefix_pages,
                                                   n_slots, qscale);
-        if (rc != LF_OK) return rc;
-        rc = launch_status("decode split");
-        if (rc != LF_OK) return rc;
+        if (rc == LF_OK) rc = launch_status("decode split");
+        if (rc != LF_OK) {
+            if (overlap) cudaStreamWaitEvent(st, side->join, 0);   // keep the fork closed
+            return rc;
+        }
     }
     if (prof) LF_CHECK_CUDA(cudaEventRecord(g_prof_end, st));
+    if (overlap) LF_CHECK_CUDA(cudaStreamWaitEvent(st, side->join, 0));   // prefix partials ready
     dim3 cgrid(num_q_heads, num_seqs);
     if (head_dim == 128)
         decode::combine_kernel<128><<<cgrid, 32, 0, st>>>(po, pml, seq_lens, out, lse, num_q_heads,
@@ -429,7 +478,6 @@ extern "C" int lf_decode_fwd_gather(const lf_bf16* q, const lf_bf16* k_pages,
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[LF_DECODE_NOALLOC_SCRATCH_BYTES];
 
-#include <mutex>
 
 namespace lf {
 namespace decode {
