@@ -10,27 +10,30 @@
 //   warp 0        TMA producer: per item, Q of both tiles (after the previous item's last QK^T
 //                 released the Q buffer), then K and V blocks into a 2-stage ring shared by all
 //                 items (running block counter g);
-//   warp 1        TMEM owner and MMA issuer (one thread); per key block j of an item:
+//   warp 1        TMEM owner and MMA issuer (the warp waits, one elected lane issues);
+//                 per key block j of an item:
 //                   PV(0, j) [after P_0 ready], QK(0, j+1), PV(1, j) [after P_1 ready], QK(1, j+1);
 //                 S_t(j+1) overwrites P_t(j) in TMEM only after PV(t, j) has been issued, and
 //                 tcgen05 MMAs of one thread run in issue order;
 //   warps 2-3     idle;
 //   warps 4-7     softmax + epilogue of tile 0, warps 8-11 of tile 1 (thread = query row =
-//                 TMEM lane).  Masked blocks (ragged end, causal diagonal) are rewritten in
-//                 TMEM with -inf past the visible prefix of columns; then scores are read in
-//                 two passes of 64 columns (row max, then exp2 / sum / bf16 pack) and the bf16 P
-//                 row is written over the first 64 columns of the same S buffer, where P.V reads
-//                 it as the A operand.  Scale-and-shift and row sums use packed f32x2 math, and
-//                 a quarter of the exponentials run on the FMA pipe (exp2_poly2) so MUFU does
-//                 not bound the loop.  The running max is raised only when it grows by more than
-//                 8 (log2 units), so O is rarely rescaled; O and the row sum always refer to the
-//                 same max, so the result is exact.
+//                 TMEM lane).  The whole 128-column S row comes into registers with one TMEM
+//                 round trip; masked blocks (ragged end, causal diagonal) get -inf past the
+//                 visible prefix of columns there.  Row max (three-input max), then exp2 / sum /
+//                 bf16 pack, and the bf16 P row is written over the first 64 columns of the same
+//                 S buffer, where P.V reads it as the A operand.  Scale-and-shift and row sums
+//                 use packed f32x2 math, and one exponential pair in eight runs on the FMA pipe
+//                 (exp2_poly2) to relieve the MUFU unit.  The running max is raised only when it
+//                 grows by more than 8 (log2 units), so O is rarely rescaled; O and the row sum
+//                 always refer to the same max, so the result is exact.
 // TMEM (512 columns): S0/P0 [0,128), S1/P1 [128,256), O0 [256,384), O1 [384,512).
 //
 // Barrier phases are running counters across items, so each barrier's waiters see its phases
-// strictly in order.  The next item's first P.V (which overwrites O_t) is issued only after
-// the softmax warps of tile t signalled P for that item, which they do after their epilogue
-// has read O_t.
+// strictly in order.  A tcgen05 commit signals completion of every earlier MMA of the issuing
+// thread, so S_FULL(t) for block j+1 also tells softmax t that P.V(t, j) is done (O_t may be
+// rescaled); O_DONE(t) is committed once per item, after the tile's last P.V.  The next item's
+// first P.V (which overwrites O_t) is issued only after the softmax warps of tile t signalled P
+// for that item, which they do after their epilogue has read O_t.
 //
 // Two instantiations:
 //   Dense  (prefill)  Q [B,Hq,Sq,D], K/V [B,Hkv,Sk,D]; an item = query tiles (2i, 2i+1) of one
@@ -374,61 +377,73 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                 mma_ts(tmem + kColO + t * 128, pa + kk * 8, sdesc_sw128(va + kk * 2048, kHalfBytes, 1024),
                        idesc_pv, (acc || kk > 0) ? 1u : 0u);
         };
+        // The whole warp runs this loop and every wait (each wait's result is voted, so control
+        // flow stays warp-uniform); one elected lane issues the MMAs and their commits.  Keeping
+        // the loop converged keeps the MMA operands in the uniform datapath: the same loop run
+        // by one divergent lane issued tcgen05.mma about 25% slower.
+        auto wait = [&](int b, uint32_t parity, int site) {
+            return __all_sync(0xffffffffu, mbar_wait(bar(b), parity, abort_flag, site));
+        };
         int g = 0, qi = 0, pc[2] = {0, 0};
         bool ok = true;
         for (int w = blockIdx.x; w < p.n_items && ok; w += gridDim.x) {
             const Item it = item_coords<M>(p, w, lane);
             if (it.nbk == 0) continue;
-            if (lane == 0) {
-                ok = mbar_wait(bar(Q_FULL), qi & 1, abort_flag, 3) &&
-                     mbar_wait(bar(K_FULL + (g & 1)), (g >> 1) & 1, abort_flag, 4);
-                if (ok) {
+            if (!(ok = wait(Q_FULL, qi & 1, 3) && wait(K_FULL + (g & 1), (g >> 1) & 1, 4))) break;
+            tc_fence_after();
+            if (elect_one()) {
+#pragma unroll
+                for (int t = 0; t < 2; ++t)
+                    if (it.nb[t] > 0) {
+                        qk(t, g & 1);
+                        mma_commit(bar(S_FULL + t));
+                    }
+                mma_commit(bar(K_EMPTY + (g & 1)));
+                if (it.nbk == 1) mma_commit(bar(Q_EMPTY));
+            }
+            __syncwarp();
+            for (int j = 0; j < it.nbk; ++j) {
+                const int gj = g + j, st = gj & 1;
+                const bool next = j + 1 < it.nbk;
+                // V(j) and K(j+1) are awaited lazily, right before their first use.
+                bool have_v = false, have_k = false;
+#pragma unroll
+                for (int t = 0; t < 2; ++t) {
+                    if (j >= it.nb[t]) continue;
+                    if (!have_v) {
+                        if (!(ok = wait(V_FULL + st, (gj >> 1) & 1, 6))) break;
+                        have_v = true;
+                    }
+                    if (!(ok = wait(P_FULL + t, pc[t] & 1, 5))) break;
+                    ++pc[t];
                     tc_fence_after();
-#pragma unroll
-                    for (int t = 0; t < 2; ++t)
-                        if (it.nb[t] > 0) {
-                            qk(t, g & 1);
-                            mma_commit(bar(S_FULL + t));
-                        }
-                    mma_commit(bar(K_EMPTY + (g & 1)));
-                    if (it.nbk == 1) mma_commit(bar(Q_EMPTY));
-                }
-                for (int j = 0; ok && j < it.nbk; ++j) {
-                    const int gj = g + j, st = gj & 1;
-                    const bool next = j + 1 < it.nbk;
-                    // V(j) and K(j+1) are awaited lazily, right before their first use.
-                    bool have_v = false, have_k = false;
-#pragma unroll
-                    for (int t = 0; t < 2; ++t) {
-                        if (j >= it.nb[t]) continue;
-                        if (!have_v) {
-                            if (!(ok = mbar_wait(bar(V_FULL + st), (gj >> 1) & 1, abort_flag, 6))) break;
-                            have_v = true;
-                        }
-                        if (!(ok = mbar_wait(bar(P_FULL + t), pc[t] & 1, abort_flag, 5))) break;
-                        ++pc[t];
-                        tc_fence_after();
+                    const bool more = j + 1 < it.nb[t];
+                    if (elect_one()) {
                         pv(t, st, j > 0);
-                        mma_commit(bar(O_DONE + t));
-                        if (j + 1 < it.nb[t]) {
-                            if (!have_k) {
-                                if (!(ok = mbar_wait(bar(K_FULL + (st ^ 1)), ((gj + 1) >> 1) & 1,
-                                                     abort_flag, 4)))
-                                    break;
-                                tc_fence_after();
-                                have_k = true;
-                            }
+                        if (!more) mma_commit(bar(O_DONE + t));   // O_t final
+                    }
+                    __syncwarp();
+                    if (more) {
+                        if (!have_k) {
+                            if (!(ok = wait(K_FULL + (st ^ 1), ((gj + 1) >> 1) & 1, 4))) break;
+                            tc_fence_after();
+                            have_k = true;
+                        }
+                        if (elect_one()) {
                             qk(t, st ^ 1);
                             mma_commit(bar(S_FULL + t));
                         }
+                        __syncwarp();
                     }
-                    if (!ok) break;
+                }
+                if (!ok) break;
+                if (elect_one()) {
                     mma_commit(bar(V_EMPTY + st));
                     if (next) mma_commit(bar(K_EMPTY + (st ^ 1)));
                     if (j + 2 == it.nbk) mma_commit(bar(Q_EMPTY));   // last QK^T of the item issued
                 }
+                __syncwarp();
             }
-            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             g += it.nbk;
             ++qi;
         }
@@ -441,6 +456,7 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
         const uint32_t s_col = tmem + lane_off + kColS + t * 128;
         const uint32_t o_col = tmem + lane_off + kColO + t * 128;
         int cnt = 0;        // blocks this tile has processed, across items
+        int ocnt = 0;       // items with blocks this tile has finished (O_DONE phases)
         bool ok = true;
         for (int w = blockIdx.x; w < p.n_items && ok; w += gridDim.x) {
             const Item it = item_coords<M>(p, w, lane);
@@ -526,11 +542,8 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                 const float2 lsv = f2_unpack(fadd2(lsa, lsb));
                 const float lsum = lsv.x + lsv.y;
                 if (j > 0) {
-                    // PV(t, j-1) has finished (it precedes QK(t, j) in issue order); waiting on
-                    // its phase keeps O_DONE's phases consumed in order and makes O safe to scale.
-                    ok = __all_sync(0xffffffffu, mbar_wait(bar(O_DONE + t), (cnt - 1) & 1, abort_flag, 8));
-                    if (!ok) break;
-                    tc_fence_after();
+                    // PV(t, j-1) has finished: it was issued before QK(t, j), whose S_FULL
+                    // commit this warp has waited on, so O_t is safe to scale.
                     if (__any_sync(0xffffffffu, alpha != 1.f)) {
                         uint32_t r[32];
 #pragma unroll 1
@@ -554,8 +567,10 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
             }
             if (!ok) break;
             if (n_blk > 0) {
-                ok = __all_sync(0xffffffffu, mbar_wait(bar(O_DONE + t), (cnt - 1) & 1, abort_flag, 9));
+                // one O_DONE phase per item with blocks: the commit after its last P.V
+                ok = __all_sync(0xffffffffu, mbar_wait(bar(O_DONE + t), ocnt & 1, abort_flag, 9));
                 if (!ok) break;
+                ++ocnt;
                 tc_fence_after();
             }
             // ---- epilogue: read O_t (the next item's first P.V may then overwrite it) ----

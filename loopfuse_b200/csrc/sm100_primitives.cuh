@@ -141,6 +141,17 @@ __device__ __forceinline__ float2 exp2_poly2(uint64_t t2) {
                        __int_as_float(__float_as_int(pv.y) + (__float_as_int(yv.y) << 23)));
 }
 
+// True in exactly one lane of a converged warp (all 32 lanes must execute it).
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t"
+        "elect.sync _|P, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, P;\n\t}"
+        : "=r"(pred));
+    return pred != 0;
+}
+
 // max of three floats in one instruction (sm_100).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
     float d;
