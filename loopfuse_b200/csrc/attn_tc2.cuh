@@ -80,12 +80,12 @@ constexpr float kRescaleThreshold = 8.0f;
 // Which exp2 pairs of each group of 8 run as a polynomial on the FMA pipe (bit i: pair i % 8);
 // the rest use the MUFU unit.  Balances the two pipes.
 #ifndef LF_POLY_MASK
-#define LF_POLY_MASK 0x80
+#define LF_POLY_MASK 0x88
 #endif
 constexpr unsigned kPolyMask = LF_POLY_MASK;
 
 enum Bar { Q_FULL = 0, Q_EMPTY = 1, K_FULL = 2, K_EMPTY = 4, V_FULL = 6, V_EMPTY = 8, S_FULL = 10,
-           P_FULL = 12, O_DONE = 14, NUM_BARS = 16 };
+           P_FULL = 12, O_DONE = 14, P_HALF = 16, NUM_BARS = 18 };
 
 enum class Mode { Dense, Paged, Prefix };
 
@@ -224,6 +224,7 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
             mbar_init(bar(V_EMPTY + s), 1);
             mbar_init(bar(S_FULL + s), 1);
             mbar_init(bar(P_FULL + s), 4);           // one arrival per softmax warp
+            mbar_init(bar(P_HALF + s), 4);
             mbar_init(bar(O_DONE + s), 1);
         }
         *abort_flag = 0;
@@ -369,11 +370,13 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                        kk > 0);
             }
         };
-        auto pv = [&](int t, int st, bool acc) {
+        // P.V over keys [k0 * 16, k0 * 16 + BN / 2): the first half of a block runs as soon as
+        // the softmax warps have stored the first half of P.
+        auto pv = [&](int t, int st, bool acc, int k0) {
             const uint32_t va = sbase + OFF_V + st * kTileBytes;
             const uint32_t pa = tmem + kColS + t * 128;
 #pragma unroll
-            for (int kk = 0; kk < BN / 16; ++kk)
+            for (int kk = k0; kk < k0 + BN / 32; ++kk)
                 mma_ts(tmem + kColO + t * 128, pa + kk * 8, sdesc_sw128(va + kk * 2048, kHalfBytes, 1024),
                        idesc_pv, (acc || kk > 0) ? 1u : 0u);
         };
@@ -381,15 +384,17 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
         // flow stays warp-uniform); one elected lane issues the MMAs and their commits.  Keeping
         // the loop converged keeps the MMA operands in the uniform datapath: the same loop run
         // by one divergent lane issued tcgen05.mma about 25% slower.
-        auto wait = [&](int b, uint32_t parity, int site) {
-            return __all_sync(0xffffffffu, mbar_wait(bar(b), parity, abort_flag, site));
-        };
+        auto vote = [&](bool v) { return __all_sync(0xffffffffu, v); };
         int g = 0, qi = 0, pc[2] = {0, 0};
         bool ok = true;
         for (int w = blockIdx.x; w < p.n_items && ok; w += gridDim.x) {
             const Item it = item_coords<M>(p, w, lane);
             if (it.nbk == 0) continue;
-            if (!(ok = wait(Q_FULL, qi & 1, 3) && wait(K_FULL + (g & 1), (g >> 1) & 1, 4))) break;
+            {
+                const uint32_t bs[2] = {bar(Q_FULL), bar(K_FULL + (g & 1))};
+                const uint32_t ps[2] = {static_cast<uint32_t>(qi & 1), static_cast<uint32_t>((g >> 1) & 1)};
+                if (!(ok = vote(mbar_wait_all(bs, ps, abort_flag, 3)))) break;
+            }
             tc_fence_after();
             if (elect_one()) {
 #pragma unroll
@@ -405,36 +410,42 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
             for (int j = 0; j < it.nbk; ++j) {
                 const int gj = g + j, st = gj & 1;
                 const bool next = j + 1 < it.nbk;
-                // V(j) and K(j+1) are awaited lazily, right before their first use.
                 bool have_v = false, have_k = false;
 #pragma unroll
                 for (int t = 0; t < 2; ++t) {
                     if (j >= it.nb[t]) continue;
-                    if (!have_v) {
-                        if (!(ok = wait(V_FULL + st, (gj >> 1) & 1, 6))) break;
-                        have_v = true;
+                    const bool more = j + 1 < it.nb[t];
+                    // One wait point per half of P_t; the first also covers V(j) and K(j+1) when
+                    // not yet awaited (unused slots repeat the P barrier).  Keeping the waits
+                    // together keeps the issue gaps short: the MMA queue holds only a few MMAs.
+                    const uint32_t pbar = bar(P_HALF + t), ppar = pc[t] & 1;
+                    const uint32_t bs[3] = {pbar, have_v ? pbar : bar(V_FULL + st),
+                                            (more && !have_k) ? bar(K_FULL + (st ^ 1)) : pbar};
+                    const uint32_t ps[3] = {ppar, have_v ? ppar : static_cast<uint32_t>((gj >> 1) & 1),
+                                            (more && !have_k) ? static_cast<uint32_t>(((gj + 1) >> 1) & 1) : ppar};
+                    if (!(ok = vote(mbar_wait_all(bs, ps, abort_flag, 5)))) break;
+                    have_v = true;
+                    have_k = have_k || more;
+                    tc_fence_after();
+                    if (elect_one()) pv(t, st, j > 0, 0);
+                    __syncwarp();
+                    {
+                        const uint32_t b1[1] = {bar(P_FULL + t)};
+                        const uint32_t p1[1] = {ppar};
+                        if (!(ok = vote(mbar_wait_all(b1, p1, abort_flag, 5)))) break;
                     }
-                    if (!(ok = wait(P_FULL + t, pc[t] & 1, 5))) break;
                     ++pc[t];
                     tc_fence_after();
-                    const bool more = j + 1 < it.nb[t];
                     if (elect_one()) {
-                        pv(t, st, j > 0);
-                        if (!more) mma_commit(bar(O_DONE + t));   // O_t final
-                    }
-                    __syncwarp();
-                    if (more) {
-                        if (!have_k) {
-                            if (!(ok = wait(K_FULL + (st ^ 1), ((gj + 1) >> 1) & 1, 4))) break;
-                            tc_fence_after();
-                            have_k = true;
-                        }
-                        if (elect_one()) {
+                        pv(t, st, true, BN / 32);
+                        if (more) {
                             qk(t, st ^ 1);
                             mma_commit(bar(S_FULL + t));
+                        } else {
+                            mma_commit(bar(O_DONE + t));   // O_t final
                         }
-                        __syncwarp();
                     }
+                    __syncwarp();
                 }
                 if (!ok) break;
                 if (elect_one()) {
@@ -514,49 +525,57 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                 const float m_new = (m_blk > m_run + kRescaleThreshold) ? m_blk : m_run;
                 const float alpha = (m_new == m_run) ? 1.f : fast_exp2(m_run - m_new);
                 const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-                // exp2, row sum and bf16 P, packed in place: pair i (columns 2i, 2i+1) becomes
-                // r[i], so P of score columns [0, 128) lands in TMEM columns [0, 64) of this
-                // S buffer.  The pairs kPolyMask selects run on the FMA pipe.
-                const uint64_t c2 = f2_pack(p.c, p.c), nm2 = f2_pack(-m_use, -m_use);
-                uint64_t lsa = f2_pack(0.f, 0.f), lsb = f2_pack(0.f, 0.f);
-#pragma unroll
-                for (int i = 0; i < BN / 2; ++i) {
-                    const uint64_t a = ffma2(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])),
-                                             c2, nm2);
-                    float2 e;
-                    uint32_t pb;
-                    if ((kPolyMask >> (i & 7)) & 1u) {
-                        e = exp2_poly2(a);
-                        pb = pack_bf16x2(e.x, e.y);
-                    } else {
-                        const float2 av = f2_unpack(a);
-                        e = make_float2(fast_exp2(av.x), fast_exp2(av.y));
-                        pb = pack_bf16x2(e.x, e.y);
-                    }
-                    if (i & 1) lsb = fadd2(lsb, f2_pack(e.x, e.y));
-                    else lsa = fadd2(lsa, f2_pack(e.x, e.y));
-                    r[i] = pb;
-                }
-                tmem_st32(s_col, chunk(0));
-                tmem_st32(s_col + 32, chunk(1));
-                const float2 lsv = f2_unpack(fadd2(lsa, lsb));
-                const float lsum = lsv.x + lsv.y;
                 if (j > 0) {
                     // PV(t, j-1) has finished: it was issued before QK(t, j), whose S_FULL
-                    // commit this warp has waited on, so O_t is safe to scale.
+                    // commit this warp has waited on, so O_t is safe to scale -- before this
+                    // block's first P.V, which the P_HALF arrival below releases.
                     if (__any_sync(0xffffffffu, alpha != 1.f)) {
-                        uint32_t r[32];
+                        // 8 columns at a time: the S row is live in registers here
+                        uint32_t o8[8];
 #pragma unroll 1
-                        for (int cc = 0; cc < HD / 32; ++cc) {
-                            tmem_ld32(o_col + cc * 32, r);
+                        for (int cc = 0; cc < HD / 8; ++cc) {
+                            tmem_ld8(o_col + cc * 8, o8);
                             tmem_wait_ld();
 #pragma unroll
-                            for (int i = 0; i < 32; ++i)
-                                r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-                            tmem_st32(o_col + cc * 32, r);
+                            for (int i = 0; i < 8; ++i)
+                                o8[i] = __float_as_uint(__uint_as_float(o8[i]) * alpha);
+                            tmem_st8(o_col + cc * 8, o8);
                         }
                     }
                 }
+                // exp2, row sum and bf16 P, packed in place: pair i (columns 2i, 2i+1) becomes
+                // r[i], so P of score columns [0, 128) lands in TMEM columns [0, 64) of this
+                // S buffer.  The pairs kPolyMask selects run on the FMA pipe.  The first half
+                // of P is stored and signalled (P_HALF) before the second half is computed, so
+                // its P.V overlaps the rest of this softmax.
+                const uint64_t c2 = f2_pack(p.c, p.c), nm2 = f2_pack(-m_use, -m_use);
+                uint64_t lsa = f2_pack(0.f, 0.f), lsb = f2_pack(0.f, 0.f);
+                auto pair = [&](int i) {
+                    const uint64_t a = ffma2(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])),
+                                             c2, nm2);
+                    float2 e;
+                    if ((kPolyMask >> (i & 7)) & 1u) {
+                        e = exp2_poly2(a);
+                    } else {
+                        const float2 av = f2_unpack(a);
+                        e = make_float2(fast_exp2(av.x), fast_exp2(av.y));
+                    }
+                    if (i & 1) lsb = fadd2(lsb, f2_pack(e.x, e.y));
+                    else lsa = fadd2(lsa, f2_pack(e.x, e.y));
+                    r[i] = pack_bf16x2(e.x, e.y);
+                };
+#pragma unroll
+                for (int i = 0; i < BN / 4; ++i) pair(i);
+                tmem_st32(s_col, chunk(0));
+                tmem_wait_st();                      // also orders any O rescale above
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(P_HALF + t));
+#pragma unroll
+                for (int i = BN / 4; i < BN / 2; ++i) pair(i);
+                tmem_st32(s_col + 32, chunk(1));
+                const float2 lsv = f2_unpack(fadd2(lsa, lsb));
+                const float lsum = lsv.x + lsv.y;
                 l_run = l_run * alpha + lsum;
                 m_run = m_new;
                 tmem_wait_st();

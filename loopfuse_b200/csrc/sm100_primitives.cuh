@@ -67,6 +67,31 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
     }
 }
 
+// Wait for several barrier phases at once: the first round polls all of them back to back, so
+// barriers that have already completed cost one round trip together.  Same time limit and error
+// reporting as mbar_wait.
+template <int N>
+__device__ __forceinline__ bool mbar_wait_all(const uint32_t (&bars)[N], const uint32_t (&parity)[N],
+                                              int* err, int site, uint64_t limit_ns = 2000000000ull) {
+    uint32_t pending = 0;
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+        if (!mbar_try_wait(bars[i], parity[i])) pending |= 1u << i;
+    if (pending == 0) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+#pragma unroll
+        for (int i = 0; i < N; ++i)
+            if (((pending >> i) & 1u) && mbar_try_wait(bars[i], parity[i])) pending &= ~(1u << i);
+        if (pending == 0) return true;
+        if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+        if (global_timer_ns() - t0 > limit_ns) {
+            atomicCAS(err, 0, site);
+            return false;
+        }
+    }
+}
+
 // ---- TMA ------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -227,6 +252,20 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
           "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr)
         : "memory");
+}
+
+// 8 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                   "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+                 "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
 }
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
