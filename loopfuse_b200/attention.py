@@ -62,14 +62,15 @@ def prefill_attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cau
 def prefill_paged(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torch.Tensor,
                   block_table: torch.Tensor, cu_seqlens_q: torch.Tensor, seqlens_k: torch.Tensor,
                   max_seqlen_q: int, causal: bool = True, scale: Optional[float] = None,
-                  return_lse: bool = False):
+                  return_lse: bool = False, out: Optional[torch.Tensor] = None):
     """Attention of newly appended tokens over each session's cached paged K/V.
 
     ``q [T, Hq, D]``: the new tokens of N sessions back to back, session ``n`` owning rows
     ``cu_seqlens_q[n] .. cu_seqlens_q[n+1]``; ``k_pages, v_pages [P, Hkv, 16, D]`` (one layer,
     new tokens already appended); ``block_table [N, max_pages]``; ``seqlens_k [N]`` context
     lengths including the new tokens.  Causal with the queries at the end of their session.
-    Returns ``o [T, Hq, D]`` (and ``lse [T, Hq]``).
+    Returns ``o [T, Hq, D]`` (and ``lse [T, Hq]``); ``out``, when given, is a contiguous
+    ``[T, Hq, D]`` bf16 tensor that receives ``o``.
     """
     for t, n in ((q, "q"), (k_pages, "k_pages"), (v_pages, "v_pages")):
         _require(t, n)
@@ -82,7 +83,13 @@ def prefill_paged(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torch.Tensor,
     if page != LF_PAGE_SIZE or Dk != D or cu_seqlens_q.shape != (N + 1,) or seqlens_k.shape != (N,):
         raise LoopfuseError(_lib.LF_EINVAL, "prefill_paged: inconsistent shapes")
     scale = D ** -0.5 if scale is None else float(scale)
-    o = torch.empty_like(q)
+    if out is None:
+        o = torch.empty_like(q)
+    else:
+        _require(out, "out")
+        if out.shape != q.shape:
+            raise LoopfuseError(_lib.LF_EINVAL, "prefill_paged: out must have q's shape")
+        o = out
     lse = torch.empty((T, Hq), dtype=torch.float32, device=q.device) if return_lse else None
     _lib.call("lf_prefill_paged_fwd", q.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(),
               block_table.data_ptr(), cu_seqlens_q.data_ptr(), seqlens_k.data_ptr(), o.data_ptr(),

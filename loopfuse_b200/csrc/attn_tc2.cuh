@@ -67,6 +67,8 @@ constexpr int BM = 128;
 constexpr int BN = 128;
 constexpr int kMaxHD = 128;                       // buffers are sized for head_dim 128
 constexpr int kThreads = 384;
+constexpr uint32_t kRegsControl = 96, kRegsSoftmax = 200;   // per thread, after the split
+static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= kThreads * 168, "register split");
 constexpr uint32_t kTileBytes = BM * kMaxHD * 2;  // 32 KB
 constexpr uint32_t kHalfBytes = kTileBytes / 2;   // 16 KB: [128 rows][64 dims]
 constexpr uint32_t kPageBoxBytes = 16 * 64 * 2;   // 2 KB: [16 rows][64 dims]
@@ -239,8 +241,15 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // Registers move from warpgroup 0 (TMA, MMA and two idle warps) to the two softmax
+    // warpgroups, whose whole-row S registers otherwise spill: 128 x 96 + 256 x 200 = 63488, within
+    // the 384 x 168 = 64512 the block is launched with.
+    // Each role adjusts its own budget at the top of its branch.
+    static_assert(kThreads == 384, "register split sized for 384 threads");
+
     if (warp == 0) {
         // ---------------- TMA producer ----------------
+        setmaxnreg_dec<kRegsControl>();
         if (lane == 0) {
             tma_prefetch_desc(&tmq);
             tma_prefetch_desc(&tmk);
@@ -358,6 +367,7 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
         __syncwarp();
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
+        setmaxnreg_dec<kRegsControl>();
         constexpr uint32_t idesc_qk = idesc_bf16_f32(BM, BN, false);
         constexpr uint32_t idesc_pv = idesc_bf16_f32(BM, HD, true);
         auto qk = [&](int t, int st) {
@@ -459,8 +469,11 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
             ++qi;
         }
         __syncwarp();
-    } else if (warp >= 4) {
+    } else if (warp < 4) {
+        setmaxnreg_dec<kRegsControl>();                  // idle warps of warpgroup 0
+    } else {
         // ---------------- softmax + epilogue (tile t) ----------------
+        setmaxnreg_inc<kRegsSoftmax>();
         const int t = (warp - 4) >> 2;
         const int row = ((warp - 4) & 3) * 32 + lane;
         const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;

@@ -166,6 +166,17 @@ __device__ __forceinline__ float2 exp2_poly2(uint64_t t2) {
                        __int_as_float(__float_as_int(pv.y) + (__float_as_int(yv.y) << 23)));
 }
 
+// Register budget of the executing warpgroup (all four warps execute the same instruction).
+// A block's warpgroups may trade registers only within the total it was launched with.
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // True in exactly one lane of a converged warp (all 32 lanes must execute it).
 __device__ __forceinline__ bool elect_one() {
     uint32_t pred = 0;

@@ -49,6 +49,9 @@ def test_paged_prefill_matches_oracle(hq, hkv, D):
     cu = torch.tensor([0] + list(torch.tensor(new_counts).cumsum(0)), dtype=torch.int32, device="cuda")
     kp, vp = pool.layer_pages(layer)
     o, lse = att.prefill_paged(q, kp, vp, table, cu, lens, max(new_counts), return_lse=True)
+    into = torch.full_like(q, float("nan"))
+    att.prefill_paged(q, kp, vp, table, cu, lens, max(new_counts), out=into)
+    assert torch.equal(into, o)                               # the out= path writes the same bits
     off = 0
     for i, s in enumerate(states):
         n = new_counts[i]
