@@ -22,8 +22,10 @@
 //                 visible prefix of columns there.  Row max (three-input max), then exp2 / sum /
 //                 bf16 pack, and the bf16 P row is written over the first 64 columns of the same
 //                 S buffer, where P.V reads it as the A operand.  Scale-and-shift and row sums
-//                 use packed f32x2 math, and one exponential pair in eight runs on the FMA pipe
-//                 (exp2_poly2) to relieve the MUFU unit.  The running max is raised only when it
+//                 use packed f32x2 math, and two exponential pairs in eight run on the FMA pipe
+//                 (exp2_poly2) to relieve the MUFU unit.  The first
+//                 half of P is stored and signalled (P_HALF) before the second half is computed,
+//                 so its P.V overlaps the rest of the softmax.  The running max is raised only when it
 //                 grows by more than 8 (log2 units), so O is rarely rescaled; O and the row sum
 //                 always refer to the same max, so the result is exact.
 // TMEM (512 columns): S0/P0 [0,128), S1/P1 [128,256), O0 [256,384), O1 [384,512).
@@ -79,17 +81,17 @@ constexpr uint32_t OFF_BAR = OFF_V + 2 * kTileBytes;
 constexpr uint32_t kSmemBytes = OFF_BAR + 256 + 1024;
 constexpr uint32_t kColS = 0, kColO = 256, kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;
-// Which exp2 pairs of each group of 8 run as a polynomial on the FMA pipe (bit i: pair i % 8);
-// the rest use the MUFU unit.  Balances the two pipes.
-#ifndef LF_POLY_MASK
-#define LF_POLY_MASK 0x88
-#endif
-constexpr unsigned kPolyMask = LF_POLY_MASK;
 
 enum Bar { Q_FULL = 0, Q_EMPTY = 1, K_FULL = 2, K_EMPTY = 4, V_FULL = 6, V_EMPTY = 8, S_FULL = 10,
            P_FULL = 12, O_DONE = 14, P_HALF = 16, NUM_BARS = 18 };
 
 enum class Mode { Dense, Paged, Prefix };
+
+// Which exp2 pairs of each group of 8 run as a polynomial on the FMA pipe (bit i: pair i % 8);
+// the rest use the MUFU unit.  Two in eight measured best for the dense prefill (A/B over 1/8 to
+// 4/8).  Every mode uses the same share, so a paged prefill over a contiguous context gives the
+// dense prefill's bits.
+constexpr unsigned kPolyMask = 0x88u;
 
 struct Params {
     float c;
