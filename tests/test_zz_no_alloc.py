@@ -29,10 +29,12 @@ def _noalloc(w, out, lse):
         w.block_table.shape[1], D ** -0.5, torch.cuda.current_stream().cuda_stream)
 
 
-@pytest.mark.parametrize("prefix_tokens", [0, 512])
-def test_noalloc_matches_workspace_entry_point_twice(prefix_tokens):
+@pytest.mark.parametrize("prefix_tokens,hq,hkv,d", [(0, 32, 8, 128), (512, 32, 8, 128),
+                                                     (0, 8, 2, 64), (256, 12, 12, 64)])
+def test_noalloc_matches_workspace_entry_point_twice(prefix_tokens, hq, hkv, d):
     lengths = [1, 16, 17, 300, 2048, 5000, 9000, 700, 12000, 64, 4096, 3333]
-    w = decode_inputs(N=len(lengths), lengths=lengths, prefix_tokens=prefix_tokens, seed=21)
+    w = decode_inputs(N=len(lengths), Hq=hq, Hkv=hkv, D=d, lengths=lengths,
+                      prefix_tokens=prefix_tokens, seed=21)
     ref, ref_lse = att.paged_decode(w.q, w.k_pages, w.v_pages, w.block_table, w.seq_lens,
                                     num_prefix_pages=w.n_prefix_pages, return_lse=True)
     for _ in range(2):
