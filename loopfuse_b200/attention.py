@@ -101,12 +101,14 @@ def prefill_paged(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torch.Tensor,
 def default_pages_per_split(num_seqs: int, num_kv_heads: int, max_pages: int,
                             num_prefix_pages: int = 0) -> int:
     """Split size for the sessions' own pages (the shared prefix is read separately): enough
-    CTAs for several waves on 148 SMs, 8 to 128 pages each.  ``max_pages`` is the block-table
-    width, each session's capacity; sessions are taken to be half full on average."""
+    CTAs for several waves on 148 SMs, 32 to 128 pages each.  ``max_pages`` is the block-table
+    width, each session's capacity; sessions are taken to be half full on average.  The floor
+    of 32 keeps small batches from launching many short or empty splits: the grid is sized for
+    the table's capacity, and three split CTAs fit on an SM at a time."""
     target_ctas = SM_COUNT * 3 * 8
     own = max(1, (max_pages - num_prefix_pages) // 2)
     per = max(1, (num_seqs * num_kv_heads * own) // target_ctas)
-    pps = 8
+    pps = 32
     while pps < per and pps < 128:
         pps *= 2
     return pps

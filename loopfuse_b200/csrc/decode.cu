@@ -374,25 +374,27 @@ static int decode_impl(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* 
     const bool overlap = num_prefix_pages > 0 && max_split > 0;
     std::unique_lock<std::mutex> side_lock(g_side_mu, std::defer_lock);
     SideStream* side = nullptr;
-    if (num_prefix_pages > 0) {
-        cudaStream_t pst = st;
-        if (overlap) {
-            side_lock.lock();
-            int rc = side_stream(&side);
-            if (rc != LF_OK) return rc;
-            LF_CHECK_CUDA(cudaEventRecord(side->fork, st));
-            LF_CHECK_CUDA(cudaStreamWaitEvent(side->s, side->fork, 0));
-            pst = side->s;
-        }
-        int rc = decode::launch_prefix(q16, k_pages, v_pages, block_table, seq_lens, po, pml,
-                                       num_seqs, num_q_heads, num_kv_heads, head_dim, num_pages,
-                                       max_pages, num_prefix_pages, decode::prefix_chunk_pages(pages_per_split), n_slots, max_split,
-                                       qscale, pst);
-        if (overlap) cudaEventRecord(side->join, side->s);
-        if (rc != LF_OK) {
-            if (overlap) cudaStreamWaitEvent(st, side->join, 0);   // keep the fork closed
-            return rc;
-        }
+    // With both passes, the split kernel goes first and the prefix pass forks onto the side
+    // stream from the same point: the split's many small CTAs take the SMs first and the
+    // prefix's persistent CTAs fill in as they drain (measured faster than the reverse order,
+    // in which the prefix CTAs hold whole SMs while the split waits).
+    if (overlap) {
+        side_lock.lock();
+        int rc = side_stream(&side);
+        if (rc != LF_OK) return rc;
+        LF_CHECK_CUDA(cudaEventRecord(side->fork, st));
+        LF_CHECK_CUDA(cudaStreamWaitEvent(side->s, side->fork, 0));
+    }
+    auto prefix_pass = [&](cudaStream_t pst) {
+        return decode::launch_prefix(q16, k_pages, v_pages, block_table, seq_lens, po, pml,
+                                     num_seqs, num_q_heads, num_kv_heads, head_dim, num_pages,
+                                     max_pages, num_prefix_pages,
+                                     decode::prefix_chunk_pages(pages_per_split), n_slots,
+                                     max_split, qscale, pst);
+    };
+    if (num_prefix_pages > 0 && !overlap) {
+        int rc = prefix_pass(st);
+        if (rc != LF_OK) return rc;
     }
     const bool prof = g_prof_begin != nullptr && g_prof_end != nullptr;
     if (prof) LF_CHECK_CUDA(cudaEventRecord(g_prof_begin, st));
@@ -410,7 +412,18 @@ static int decode_impl(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* 
                                                   n_slots, qscale);
         if (rc == LF_OK) rc = launch_status("decode split");
         if (rc != LF_OK) {
-            if (overlap) cudaStreamWaitEvent(st, side->join, 0);   // keep the fork closed
+            if (overlap) {                                    // keep the fork closed
+                cudaEventRecord(side->join, side->s);
+                cudaStreamWaitEvent(st, side->join, 0);
+            }
+            return rc;
+        }
+    }
+    if (overlap) {
+        const int rc = prefix_pass(side->s);
+        cudaEventRecord(side->join, side->s);
+        if (rc != LF_OK) {
+            cudaStreamWaitEvent(st, side->join, 0);           // keep the fork closed
             return rc;
         }
     }
