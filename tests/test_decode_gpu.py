@@ -94,3 +94,14 @@ def test_decode_rejects_bad_arguments():
         att.paged_decode(w.q.float(), w.k_pages, w.v_pages, w.block_table, w.seq_lens)
     with pytest.raises(RuntimeError):
         att.paged_decode(w.q.cpu(), w.k_pages, w.v_pages, w.block_table, w.seq_lens)
+
+
+def test_decode_sessions_entirely_inside_the_shared_prefix():
+    """Every session's context lies within the shared prefix, so the table has no own pages and
+    only the prefix pass runs (no split kernel)."""
+    lengths = [1024, 17, 160, 1000, 1, 512]
+    w = decode_inputs(N=len(lengths), lengths=lengths, prefix_tokens=1024, seed=9)
+    assert w.block_table.shape[1] == w.n_prefix_pages
+    o = att.paged_decode(w.q, w.k_pages, w.v_pages, w.block_table, w.seq_lens,
+                         num_prefix_pages=w.n_prefix_pages)
+    _check(o, _oracle(w)[0], "prefix only")
