@@ -57,6 +57,13 @@ const char* lf_last_error(void);
  * counterpart: the reference kernels have no device-side error reporting. */
 int lf_device_status(int* out);
 
+/* Runs, on the given stream, the bounded barrier wait that every pipelined kernel here uses,
+ * on a barrier that nothing arrives at, giving up after timeout_us (1..100000).  The expiry is
+ * recorded in the device error word exactly like a kernel's (site code 177), so a caller can
+ * check the failure path: lf_device_status() then reports it, and the context stays usable.
+ * No reference counterpart (diagnostic). */
+int lf_selftest_bounded_wait(unsigned timeout_us, void* stream);
+
 /* ---- prefill attention --------------------------------------------------
  * Replaces prefill_attention_fwd (kernels/triton/prefill_attn.py:127-168) and
  * the host launcher loopfuse_agent_prefill (kernels/cuda/async_prefill.cu:220-236).

@@ -7,7 +7,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_int64, c_size_t, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_int64, c_size_t, c_uint, c_void_p
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "liblf_sm100.so")
 
@@ -45,6 +45,7 @@ _SIGS = {
     "lf_version": [],
     "lf_last_error": [],
     "lf_device_status": [POINTER(c_int)],
+    "lf_selftest_bounded_wait": [c_uint, _P],
     "lf_prefill_fwd": [_P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, c_int, c_float,
                        c_int, _P],
     "lf_prefill_paged_fwd": [_P, _P, _P, _P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int,
