@@ -69,7 +69,7 @@ constexpr int BM = 128;
 constexpr int BN = 128;
 constexpr int kMaxHD = 128;                       // buffers are sized for head_dim 128
 constexpr int kThreads = 384;
-constexpr uint32_t kRegsControl = 96, kRegsSoftmax = 200;   // per thread, after the split
+constexpr uint32_t kRegsControl = 88, kRegsSoftmax = 208;   // per thread, after the split
 static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= kThreads * 168, "register split");
 constexpr uint32_t kTileBytes = BM * kMaxHD * 2;  // 32 KB
 constexpr uint32_t kHalfBytes = kTileBytes / 2;   // 16 KB: [128 rows][64 dims]
@@ -244,7 +244,7 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
     const uint32_t tmem = *tmem_slot;
 
     // Registers move from warpgroup 0 (TMA, MMA and two idle warps) to the two softmax
-    // warpgroups, whose whole-row S registers otherwise spill: 128 x 96 + 256 x 200 = 63488, within
+    // warpgroups, whose whole-row S registers otherwise spill: 128 x 88 + 256 x 208 = 64512, within
     // the 384 x 168 = 64512 the block is launched with.
     // Each role adjusts its own budget at the top of its branch.
     static_assert(kThreads == 384, "register split sized for 384 threads");
