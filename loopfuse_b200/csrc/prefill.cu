@@ -7,6 +7,8 @@
 // SM) walk pairs of adjacent 128-row query tiles of one (batch, query head), heavy pairs first.
 //
 // This file also launches the core's Prefix instantiation for the decode's shared-prefix pass.
+#include <atomic>
+
 #include "attn_tc2.cuh"
 #include "tmap.cuh"
 
@@ -14,14 +16,19 @@ using namespace lf;
 
 namespace {
 
+// The dynamic shared-memory opt-in is a per-device setting of the kernel, so it is made once
+// for each device this process launches on (setting it twice is harmless).
 template <lf::tc2::Mode M, int HD>
 int set_smem_attr() {
-    static bool done = false;
-    if (!done) {
+    static std::atomic<uint64_t> done{0};
+    int dev = 0;
+    LF_CHECK_CUDA(cudaGetDevice(&dev));
+    const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
+    if (bit == 0 || (done.load() & bit) == 0) {
         LF_CHECK_CUDA(cudaFuncSetAttribute(lf::tc2::attn2_kernel<M, HD>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)lf::tc2::kSmemBytes));
-        done = true;
+        done.fetch_or(bit);
     }
     return LF_OK;
 }
@@ -201,12 +208,8 @@ int launch_prefix_tc(const uint16_t* q, const uint16_t* kp, const uint16_t* vp, 
     rc = encode_bf16_map(&mv, vp, 3, pdims, pstr, pbox);
     if (rc) return rc;
 
-    static bool attr_set = false;
-    if (!attr_set) {
-        LF_CHECK_CUDA(cudaFuncSetAttribute(attn2_kernel<Mode::Prefix, 128>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
-        attr_set = true;
-    }
+    int rc0 = set_smem_attr<Mode::Prefix, 128>();
+    if (rc0) return rc0;
     Params p{};
     p.c = qscale;
     p.Hkv = Hkv;
