@@ -47,3 +47,19 @@ def test_host_side_validation_errors():
     assert rc == _lib.LF_EINVAL          # unaligned pointers rejected before any launch
     m = _lib.PoolMeta()
     assert lib.lf_pool_init(ctypes.byref(m), None) == _lib.LF_EINVAL
+
+
+def test_selftest_rejects_out_of_range_limits_before_any_launch():
+    lib = _lib.lib()
+    assert lib.lf_selftest_bounded_wait(0, None) == _lib.LF_EINVAL
+    assert b"timeout_us" in lib.lf_last_error()
+    assert lib.lf_selftest_bounded_wait(100001, None) == _lib.LF_EINVAL
+
+
+def test_default_split_size_is_a_power_of_two_between_32_and_128_pages():
+    from loopfuse_b200.attention import default_pages_per_split
+    for n, hkv, max_pages, npre in [(1, 8, 64, 0), (64, 8, 319, 256), (256, 8, 2048, 128),
+                                    (512, 8, 600, 256), (8, 2, 5000, 0)]:
+        pps = default_pages_per_split(n, hkv, max_pages, npre)
+        assert pps in (32, 64, 128), (n, hkv, max_pages, npre, pps)
+    assert default_pages_per_split(256, 8, 2048, 128) == 128      # the 256-session decode
