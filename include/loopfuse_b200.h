@@ -50,11 +50,14 @@ typedef uint16_t lf_bf16;
 const char* lf_version(void);
 const char* lf_last_error(void);
 
-/* Reads and clears the library's device-side error word (synchronous).  A
+/* Reads and clears the library's device-side error report (synchronous).  A
  * kernel whose bounded wait gave up (a pipeline barrier that never completed)
- * records a non-zero site code there instead of hanging; *out == 0 means no
- * kernel has reported a failure since the last call.  No reference
- * counterpart: the reference kernels have no device-side error reporting. */
+ * or that met a bad page id records a non-zero site code instead of hanging or
+ * faulting; *out == 0 means no kernel has reported a failure since the last
+ * call.  Each source file of the library keeps its own error word: one call
+ * returns and clears one report, so a caller that wants them all calls until
+ * *out == 0.  No reference counterpart: the reference kernels have no
+ * device-side error reporting. */
 int lf_device_status(int* out);
 
 /* Runs, on the given stream, the bounded barrier wait that every pipelined kernel here uses,
@@ -113,6 +116,15 @@ int lf_prefill_paged_fwd(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16
  * replaced by page 0; either is reported through lf_device_status(). */
 int lf_decode_workspace_size(int num_seqs, int num_q_heads, int head_dim, int max_pages,
                              int pages_per_split, int num_prefix_pages, size_t* bytes);
+
+/* Default pages_per_split for lf_decode_fwd: enough split CTAs for several waves
+ * on sm_count SMs (sm_count <= 0: the current device's count), with sessions
+ * taken to be half full, 32 to 128 pages per split.  Host-only when sm_count >
+ * 0.  The reference's decode has no split (one program per (batch, head),
+ * kernels/triton/decode_attn.py:159-171); this is the grid choice that
+ * replaces it. */
+int lf_decode_default_split(int num_seqs, int num_kv_heads, int max_pages, int num_prefix_pages,
+                            int sm_count, int* pages_per_split);
 int lf_decode_fwd(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* v_pages,
                   const int32_t* block_table, const int32_t* seq_lens, int num_prefix_pages,
                   lf_bf16* o, float* lse, void* workspace, size_t workspace_bytes,
@@ -150,12 +162,14 @@ int lf_ipc_close(void* base);
  * exit), so callers that cannot allocate device memory -- a foreign-language
  * binding without a device allocator, or a loop whose allocator has reserved
  * nearly all of HBM for the KV pool -- need pass only inputs and outputs.
- * No counterpart in the reference.  The split size is chosen internally to
- * fit the array; a request that does not fit even with one split per session
- * returns LF_EINVAL.  The first call on a device looks up the array's device
- * address (with that device current), so make it before any stream capture.
- * Calls share the array: calls whose kernels overlap on the GPU race and must
- * be serialised by the caller. */
+ * No counterpart in the reference.  The split size starts from
+ * lf_decode_default_split and doubles until the partials fit the array; a
+ * request that does not fit even with one split per session returns
+ * LF_EINVAL.  The first call in a CUDA context looks up the array's device
+ * address (with that context's device current) and keeps it for that
+ * context, so make the first call before any stream capture.  Calls share the
+ * array: calls whose kernels overlap on the GPU race and must be serialised
+ * by the caller. */
 #define LF_DECODE_NOALLOC_SCRATCH_BYTES (32u << 20)
 int lf_decode_fwd_noalloc(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* v_pages,
                           const int32_t* block_table, const int32_t* seq_lens,
@@ -207,7 +221,8 @@ int lf_pool_clear_status(const lf_pool_meta* m, void* stream);
 
 /* Allocation step of append: session seq_ids[i] grows by n_new[i] tokens,
  * taking ceil-page deltas from the queue head in order; start_pos[i] receives
- * its old length.  All or nothing.  seq_ids must be distinct. */
+ * its old length.  All or nothing.  seq_ids must be distinct: a repeated id
+ * is rejected with LF_EINVAL in the sticky status (nothing changes). */
 int lf_pool_reserve(const lf_pool_meta* m, const int32_t* seq_ids, const int32_t* n_new, int n,
                     int32_t* start_pos, void* stream);
 
@@ -215,7 +230,9 @@ int lf_pool_reserve(const lf_pool_meta* m, const int32_t* seq_ids, const int32_t
  * cu_tokens[i+1]-1 of k_new/v_new) goes to position start_pos[i] + t.
  * k_new element (layer l, token t, head h, dim d) is at
  * l*stride_layer + t*stride_token + h*stride_head + d (elements).  Pages are
- * [num_layers][num_pages][Hkv][16][D]. */
+ * [num_layers][num_pages][Hkv][16][D].  A row whose position has no reserved
+ * page (or an out-of-range session id) is not stored and sets the sticky
+ * status to LF_EINVAL; the other rows are stored. */
 int lf_pool_write_kv(const lf_pool_meta* m, const int32_t* seq_ids, const int32_t* start_pos,
                      const int32_t* cu_tokens, int n, int total_tokens, const void* k_new,
                      const void* v_new,

@@ -51,6 +51,7 @@ _SIGS = {
     "lf_prefill_paged_fwd": [_P, _P, _P, _P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int,
                              c_int, c_int, c_int, c_float, c_int, _P],
     "lf_decode_workspace_size": [c_int, c_int, c_int, c_int, c_int, c_int, POINTER(c_size_t)],
+    "lf_decode_default_split": [c_int, c_int, c_int, c_int, c_int, POINTER(c_int)],
     "lf_decode_fwd": [_P, _P, _P, _P, _P, c_int, _P, _P, _P, c_size_t, c_int, c_int, c_int,
                       c_int, c_int, c_int, c_int, c_float, _P],
     "lf_decode_fwd_noalloc": [_P, _P, _P, _P, _P, c_int, _P, _P, c_int, c_int, c_int, c_int,

@@ -24,7 +24,13 @@ import torch
 from . import _lib
 from ._lib import LF_PAGE_SIZE, LoopfuseError
 
-SM_COUNT = 148
+SM_COUNT = 148          # B200; the split heuristic uses the current device's count when it can
+
+
+def _sm_count() -> int:
+    if torch.cuda.is_available():
+        return torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    return SM_COUNT
 
 
 def _stream() -> int:
@@ -101,17 +107,15 @@ def prefill_paged(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torch.Tensor,
 def default_pages_per_split(num_seqs: int, num_kv_heads: int, max_pages: int,
                             num_prefix_pages: int = 0) -> int:
     """Split size for the sessions' own pages (the shared prefix is read separately): enough
-    CTAs for several waves on 148 SMs, 32 to 128 pages each.  ``max_pages`` is the block-table
-    width, each session's capacity; sessions are taken to be half full on average.  The floor
-    of 32 keeps small batches from launching many short or empty splits: the grid is sized for
-    the table's capacity, and three split CTAs fit on an SM at a time."""
-    target_ctas = SM_COUNT * 3 * 8
-    own = max(1, (max_pages - num_prefix_pages) // 2)
-    per = max(1, (num_seqs * num_kv_heads * own) // target_ctas)
-    pps = 32
-    while pps < per and pps < 128:
-        pps *= 2
-    return pps
+    CTAs for several waves on the device's SMs, 32 to 128 pages each.  ``max_pages`` is the
+    block-table width, each session's capacity; sessions are taken to be half full on average.
+    The floor of 32 keeps small batches from launching many short or empty splits: the grid is
+    sized for the table's capacity, and three split CTAs fit on an SM at a time.  The formula
+    lives in the library (``lf_decode_default_split``), shared with the no-allocation decode."""
+    out = _lib.c_int(0)
+    _lib.call("lf_decode_default_split", int(num_seqs), int(num_kv_heads), int(max_pages),
+              int(num_prefix_pages), _sm_count(), _lib.ctypes.byref(out))
+    return int(out.value)
 
 
 def decode_workspace_bytes(num_seqs: int, num_q_heads: int, head_dim: int, max_pages: int,

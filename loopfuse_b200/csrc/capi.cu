@@ -2,6 +2,7 @@
 #include "lf_common.cuh"
 
 #include <stdarg.h>
+#include <stdlib.h>
 
 namespace lf {
 
@@ -17,11 +18,19 @@ int set_error(int code, const char* fmt, ...) {
 
 void clear_error() { g_err[0] = '\0'; }
 
-static DeviceErrorReader g_readers[16];
+constexpr int kMaxReaders = 64;
+static DeviceErrorReader g_readers[kMaxReaders];
 static int g_n_readers = 0;
 
+// Runs at library load, once per translation unit.  Past the table's size a unit's reports
+// would be lost without a sign, so loading fails instead.
 bool register_device_error_reader(DeviceErrorReader fn) {
-    if (g_n_readers < 16) g_readers[g_n_readers++] = fn;
+    if (g_n_readers >= kMaxReaders) {
+        fprintf(stderr, "loopfuse_b200: more than %d device error words; raise kMaxReaders\n",
+                kMaxReaders);
+        abort();
+    }
+    g_readers[g_n_readers++] = fn;
     return true;
 }
 
@@ -32,11 +41,13 @@ extern "C" const char* lf_last_error(void) { return lf::g_err; }
 
 extern "C" int lf_device_status(int* out) {
     LF_CHECK_ARG(out != nullptr, "device_status: out is null");
+    // The first unit (in load order) holding a report gives it up; other units keep theirs for
+    // the next call, so repeated calls drain every report.
     int first = 0;
-    for (int i = 0; i < lf::g_n_readers; ++i) {
+    for (int i = 0; i < lf::g_n_readers && first == 0; ++i) {
         const int v = lf::g_readers[i]();
         if (v < 0) return lf::set_error(LF_ECUDA, "device_status: reading an error word failed");
-        if (first == 0) first = v;
+        first = v;
     }
     *out = first;
     lf::clear_error();

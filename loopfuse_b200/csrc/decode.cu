@@ -290,6 +290,58 @@ extern "C" int lf_decode_workspace_size(int num_seqs, int num_q_heads, int head_
     return LF_OK;
 }
 
+namespace lf {
+namespace decode {
+
+// SM count of the current device, looked up once per device ordinal.
+static int device_sm_count(int* out) {
+    static std::mutex mu;
+    static int cached[128] = {0};
+    int dev = 0;
+    LF_CHECK_CUDA(cudaGetDevice(&dev));
+    LF_CHECK_ARG(dev >= 0 && dev < 128, "decode: device ordinal %d out of range", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (cached[dev] == 0) {
+        int sms = 0;
+        LF_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        cached[dev] = sms;
+    }
+    *out = cached[dev];
+    return LF_OK;
+}
+
+// Default split size: enough CTAs for several waves of three split CTAs per SM (eight waves of
+// the table's capacity, with sessions taken to be half full), 32 to 128 pages per split.  The
+// floor of 32 keeps small batches from launching many short or empty splits.
+static int default_split(int num_seqs, int num_kv_heads, int max_pages, int num_prefix_pages,
+                         int sm_count) {
+    const long target_ctas = (long)sm_count * 3 * 8;
+    const long own = max(1, (max_pages - num_prefix_pages) / 2);
+    const long per = max(1L, ((long)num_seqs * num_kv_heads * own) / target_ctas);
+    int pps = 32;
+    while (pps < per && pps < 128) pps *= 2;
+    return pps;
+}
+
+}  // namespace decode
+}  // namespace lf
+
+extern "C" int lf_decode_default_split(int num_seqs, int num_kv_heads, int max_pages,
+                                       int num_prefix_pages, int sm_count, int* pages_per_split) {
+    LF_CHECK_ARG(pages_per_split != nullptr, "decode split: out pointer is null");
+    LF_CHECK_ARG(num_seqs >= 0 && num_kv_heads > 0 && max_pages > 0 && num_prefix_pages >= 0 &&
+                     num_prefix_pages <= max_pages,
+                 "decode split: bad arguments");
+    if (sm_count <= 0) {
+        const int rc = decode::device_sm_count(&sm_count);
+        if (rc != LF_OK) return rc;
+    }
+    *pages_per_split = decode::default_split(num_seqs, num_kv_heads, max_pages, num_prefix_pages,
+                                             sm_count);
+    clear_error();
+    return LF_OK;
+}
+
 // Defined in decode_prefix.cu: shared-prefix partials, one pass over the prefix pages per
 // group of sessions.
 namespace lf { namespace decode {
@@ -495,22 +547,64 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[LF_DECODE_NOALL
 namespace lf {
 namespace decode {
 
-// Device address of g_noalloc_scratch on the current device.  The symbol's host-side name is
-// only a stand-in, so the address is looked up once per device (the first call on a device does
-// this, with that device current) and cached.
+// Device address of g_noalloc_scratch in the current context.  The symbol's host-side name is
+// only a stand-in, so the address is looked up with cudaGetSymbolAddress, with the device
+// current, the first time a context calls, and kept for that context.  The cache is keyed on the
+// driver's context id, which is unique for the life of the process: a device reset or a
+// different context current on the same device gets a fresh lookup, never a stale address.
+typedef int (*CtxGetCurrentFn)(void**);
+typedef int (*CtxGetIdFn)(void*, unsigned long long*);
+
+static int current_context_id(unsigned long long* id) {
+    static std::once_flag once;
+    static CtxGetCurrentFn get_current = nullptr;
+    static CtxGetIdFn get_id = nullptr;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<CtxGetCurrentFn>(f);
+        f = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<CtxGetIdFn>(f);
+    });
+    LF_CHECK_ARG(get_current != nullptr && get_id != nullptr,
+                 "decode noalloc: the driver has no cuCtxGetCurrent / cuCtxGetId");
+    void* ctx = nullptr;
+    LF_CHECK_ARG(get_current(&ctx) == 0, "decode noalloc: cuCtxGetCurrent failed");
+    if (ctx == nullptr) {                 // nothing current yet: bind the device's primary context
+        int dev = 0;
+        LF_CHECK_CUDA(cudaGetDevice(&dev));
+        LF_CHECK_CUDA(cudaSetDevice(dev));
+        LF_CHECK_ARG(get_current(&ctx) == 0 && ctx != nullptr, "decode noalloc: no current context");
+    }
+    LF_CHECK_ARG(get_id(ctx, id) == 0, "decode noalloc: cuCtxGetId failed");
+    return LF_OK;
+}
+
 static int noalloc_scratch(void** out) {
     static std::mutex mu;
-    static void* addr[128] = {nullptr};
-    int dev = 0;
-    LF_CHECK_CUDA(cudaGetDevice(&dev));
-    LF_CHECK_ARG(dev >= 0 && dev < 128, "decode noalloc: device ordinal %d out of range", dev);
+    constexpr int kEntries = 128;
+    static unsigned long long ids[kEntries] = {0};
+    static void* addr[kEntries] = {nullptr};
+    static int next = 0;
+    unsigned long long id = 0;
+    int rc = current_context_id(&id);
+    if (rc != LF_OK) return rc;
     std::lock_guard<std::mutex> lock(mu);
-    if (addr[dev] == nullptr) {
-        void* p = nullptr;
-        LF_CHECK_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
-        addr[dev] = p;
-    }
-    *out = addr[dev];
+    for (int i = 0; i < kEntries; ++i)
+        if (addr[i] != nullptr && ids[i] == id) {
+            *out = addr[i];
+            return LF_OK;
+        }
+    void* p = nullptr;
+    LF_CHECK_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    ids[next] = id;
+    addr[next] = p;
+    next = (next + 1) % kEntries;
+    *out = p;
     return LF_OK;
 }
 
@@ -540,10 +634,12 @@ extern "C" int lf_decode_fwd_noalloc(const lf_bf16* q, const lf_bf16* k_pages,
                      num_prefix_pages <= max_pages,
                  "decode noalloc: bad page counts");
 
-    // Split size: the default heuristic, doubled until the partials fit the fixed scratch.
-    long per = (long)num_seqs * num_kv_heads * max_pages / (148L * 3 * 8);
-    int pps = 8;
-    while (pps < per && pps < 128) pps *= 2;
+    // Split size: the default (lf_decode_default_split on this device), doubled until the
+    // partials fit the fixed scratch.
+    int sms = 0;
+    int rc = decode::device_sm_count(&sms);
+    if (rc != LF_OK) return rc;
+    int pps = decode::default_split(num_seqs, num_kv_heads, max_pages, num_prefix_pages, sms);
     while (decode::partial_bytes(num_seqs, num_q_heads, head_dim, max_pages, pps, num_prefix_pages) >
                (size_t)LF_DECODE_NOALLOC_SCRATCH_BYTES &&
            pps < max_pages)
@@ -557,7 +653,7 @@ extern "C" int lf_decode_fwd_noalloc(const lf_bf16* q, const lf_bf16* k_pages,
                  num_seqs, num_q_heads, need, (unsigned)LF_DECODE_NOALLOC_SCRATCH_BYTES);
 
     void* scratch = nullptr;
-    int rc = decode::noalloc_scratch(&scratch);
+    rc = decode::noalloc_scratch(&scratch);
     if (rc != LF_OK) return rc;
 
     cudaStream_t st = static_cast<cudaStream_t>(stream);

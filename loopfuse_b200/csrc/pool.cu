@@ -44,13 +44,34 @@ __global__ void __launch_bounds__(kMetaThreads)
 reserve_kernel(Meta m, const int32_t* __restrict__ seq_ids, const int32_t* __restrict__ n_new,
                int n, int32_t* __restrict__ start_pos) {
     __shared__ int buf[32];
+    __shared__ unsigned seen[kDupBits / 32];
     if (status_of(m) != LF_OK) return;
+    // Every session may appear once: the page deltas are computed from each session's length
+    // before the call, so a repeated id would take pages twice.  A bitmap finds whether any id
+    // repeats; only then does the exact scan name the first repeat in call order.
+    int dup = 0;
+    if (m.S <= kDupBits) {
+        for (int w = threadIdx.x; w < (m.S + 31) / 32; w += kMetaThreads) seen[w] = 0u;
+        __syncthreads();
+        for (int i = threadIdx.x; i < n; i += kMetaThreads) {
+            const int s = seq_ids[i];
+            if (s < 0 || s >= m.S) continue;
+            const unsigned bit = 1u << (s & 31);
+            if (atomicOr(&seen[s >> 5], bit) & bit) dup = 1;
+        }
+        dup = -block_min(-dup, buf);
+    } else {
+        dup = 1;
+    }
     int first_bad = INT_MAX;
     long need_total = 0;
     for (int i = threadIdx.x; i < n; i += kMetaThreads) {
         const int s = seq_ids[i];
         const int t = n_new[i];
-        if (s < 0 || s >= m.S || t < 0) {
+        bool repeat = false;
+        if (dup)
+            for (int j = 0; j < i && !repeat; ++j) repeat = seq_ids[j] == s;
+        if (s < 0 || s >= m.S || t < 0 || repeat) {
             first_bad = min(first_bad, i * 8 + LF_EINVAL);
             continue;
         }
@@ -127,7 +148,17 @@ __global__ void write_kv_kernel(Meta m, const int32_t* __restrict__ seq_ids,
         }
         const int s = seq_ids[lo];
         const int pos = start_pos[lo] + (t - cu_tokens[lo]);
+        // A row without a reserved page (stale start_pos, a session that was not reserved, a
+        // bad id) is not stored: the sticky status says so and the other rows still land.
+        if (s < 0 || s >= m.S || pos < 0 || pos / LF_PAGE_SIZE >= m.M) {
+            atomicCAS(m.ctrl + LF_CTRL_STATUS, LF_OK, LF_EINVAL);
+            continue;
+        }
         const int page = m.bt[(long)s * m.M + pos / LF_PAGE_SIZE];
+        if (static_cast<unsigned>(page) >= static_cast<unsigned>(m.P)) {
+            atomicCAS(m.ctrl + LF_CTRL_STATUS, LF_OK, LF_EINVAL);
+            continue;
+        }
         const long src = l * sl + (long)t * st + (long)h * sh + vec * 8;
         const long dst = ((((long)l * m.P + page) * Hkv + h) * LF_PAGE_SIZE + pos % LF_PAGE_SIZE) * D + vec * 8;
         *reinterpret_cast<uint4*>(kp + dst) = *reinterpret_cast<const uint4*>(k_new + src);

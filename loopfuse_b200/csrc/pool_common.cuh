@@ -9,6 +9,9 @@ namespace lf {
 namespace pool {
 
 constexpr int kMetaThreads = 1024;
+// Sessions a reserve checks for repeated ids with a shared-memory bitmap (32 KB); larger
+// pools use the exact pairwise scan.
+constexpr int kDupBits = 1 << 18;
 
 struct Meta {
     int32_t* fq;

@@ -337,6 +337,9 @@ class AgentProgram:
     def ops_by_type(self, t: type) -> List[Op]:
         return [o for o in self.all_ops() if isinstance(o, t)]
 
+    def total_gpu_idle_ms(self) -> float:
+        return sum(s.total_gpu_idle_ms() for s in self.steps)
+
     def add_annotation(self, msg: str) -> None:
         self.pass_annotations.append(msg)
 

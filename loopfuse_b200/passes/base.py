@@ -41,3 +41,15 @@ class PassManager:
 
     def run(self, prog: AgentProgram) -> List[PassResult]:
         return [p.run(prog) for p in self.passes]
+
+    def run_until_fixed_point(self, prog: AgentProgram,
+                              max_iterations: int = 10) -> List[PassResult]:
+        """Run the pipeline repeatedly until a whole round changes nothing, at most
+        ``max_iterations`` rounds (reference ``passes/base.py:81-94``); returns every result."""
+        results: List[PassResult] = []
+        for _ in range(max_iterations):
+            round_results = self.run(prog)
+            results.extend(round_results)
+            if not any(r.changed for r in round_results):
+                break
+        return results

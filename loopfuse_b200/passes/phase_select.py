@@ -12,9 +12,10 @@ fallback, and the EAGER entry is the test oracle, not a runtime path.
 
 The roofline classification (``:130-144``) is kept with the reference's
 A100 constants by default, so annotations match the reference bit for bit;
-``PhaseSelectPass(hardware="b200")`` classifies against B200 figures
-measured on this hardware (STREAM-style copy 6.55 TB/s, cuBLAS bf16 GEMM
-1.62 PFLOP/s).
+``PhaseSelectPass(hardware="b200")`` classifies against the B200's measured
+peaks (``peaks.b200_peaks()``: the machine's measured copy bandwidth and
+burst bf16 GEMM throughput, or the built-in figures measured on a B200 of the
+build pool when no peaks file is present).
 """
 from __future__ import annotations
 
@@ -24,6 +25,7 @@ from typing import Callable, List
 
 from .base import Pass, PassResult
 from ..ir.dialect import AgentProgram, KernelTarget, LLMForwardOp, Phase
+from ..peaks import b200_peaks
 
 A100_PEAK_FLOPS_BF16 = 312e12
 A100_HBM_BANDWIDTH = 2.0e12
@@ -31,8 +33,9 @@ A100_RIDGE_POINT = A100_PEAK_FLOPS_BF16 / A100_HBM_BANDWIDTH
 T4_PEAK_FLOPS_FP16 = 65e12
 T4_HBM_BANDWIDTH = 320e9
 T4_RIDGE_POINT = T4_PEAK_FLOPS_FP16 / T4_HBM_BANDWIDTH
-B200_PEAK_FLOPS_BF16 = 1.62e15
-B200_HBM_BANDWIDTH = 6.55e12
+_B200 = b200_peaks()
+B200_PEAK_FLOPS_BF16 = _B200["bf16_tflops"] * 1e12
+B200_HBM_BANDWIDTH = _B200["hbm_gbs"] * 1e9
 B200_RIDGE_POINT = B200_PEAK_FLOPS_BF16 / B200_HBM_BANDWIDTH
 
 PHASE_KERNEL_MAP = {

@@ -13,8 +13,11 @@ four ``_dispatch_*`` methods are ``pass`` (``:278-281``).  Here:
   ``NotImplementedError`` -- no silent fallback.
 * Speculative prefill (``:238-249``) runs the model's prefill of the predicted
   next-step tokens on the pool's low-priority stream while the tool call's
-  host latency elapses; a miss rolls the session back by freeing the
-  speculative pages (``KVPool.fork`` keeps the confirmed prefix shared).
+  host latency elapses, on a branch forked from the session (``KVPool.fork``
+  shares the confirmed context).  The next PREFILL op compares its tokens with
+  the predicted ones: a hit adopts the branch (``KVPool.adopt``) and skips the
+  prefill, a miss releases the branch's pages.  Any other LLM op first waits
+  for the speculation, since both streams update the pool's metadata.
 * ``StepTrace`` keeps the reference's wall-clock fields and adds CUDA-event
   GPU times.
 * A ``KVFuseOp`` (``passes.kv_fusion.KVFusionPass``) arms prefix sharing by
@@ -211,6 +214,7 @@ class AgentExecutor:
                 if fuse:
                     self.kv_pool.register_prefix(kv_state, tokens[: self._fuse_len].tolist())
         else:
+            self._join_speculation()
             last = self._last_token if self._last_token is not None else 0
             out = []
             for _ in range(self.max_decode_tokens):
@@ -242,11 +246,15 @@ class AgentExecutor:
             return
         if not self.kv_pool._free_slots:
             return
+        if self._spec is not None:                  # one speculation in flight at a time
+            self._drop_speculation(kv_state)
         tokens = self.model.spec_tokens(step.step_id if step else 0)
         branch = self.kv_pool.fork(kv_state, kv_state.current_len, n=1)[0]
         kernel = self._kernel_for(LLMForwardOp(op.operands[0], op.operands[1], op.attrs,
                                                phase=Phase.PREFILL, seq_len=len(tokens)))
         done = torch.cuda.Event()
+        # The branch's pages and the context it attends to were written on this stream.
+        self.kv_pool.prefetch_stream.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(self.kv_pool.prefetch_stream):
             logits = self.model.prefill(tokens, branch, kernel)
             done.record()
@@ -265,22 +273,16 @@ class AgentExecutor:
             self.kv_pool.release(spec["branch"])
             return False
         # Adopt the speculative branch: its pages already hold the prompt's K/V.
-        branch = spec["branch"]
-        self.kv_pool.free(kv_state)
-        self._swap_sessions(kv_state, branch)
+        self.kv_pool.adopt(kv_state, spec["branch"])
         self._last_token = int(torch.argmax(spec["logits"][-1]).item())
         trace.spec_prefill_hit = True
         return True
 
-    def _swap_sessions(self, keep: KVState, branch: KVState) -> None:
-        """Make ``keep`` point at ``branch``'s block-table row; recycle the old row."""
-        pool = self.kv_pool
-        old_slot = keep.slot_id
-        del pool._active[branch.slot_id]
-        del pool._active[old_slot]
-        keep.slot_id, keep.current_len = branch.slot_id, branch.current_len
-        pool._active[keep.slot_id] = keep
-        pool._free_slots.append(old_slot)
+    def _join_speculation(self) -> None:
+        """Order this stream's next pool operations after an in-flight speculative prefill:
+        both streams update the same pool metadata."""
+        if self._spec is not None:
+            torch.cuda.current_stream().wait_event(self._spec["event"])
 
     def _drop_speculation(self, kv_state: KVState) -> None:
         if self._spec is not None:

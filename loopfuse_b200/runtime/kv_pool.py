@@ -254,6 +254,8 @@ class KVPool:
             if s.current_len + n > self.max_seq_len:
                 raise RuntimeError(f"KV cache overflow: current_len={s.current_len} + "
                                    f"seq_new={n} > max_seq_len={self.max_seq_len}")
+        if len({s.slot_id for s in states}) != len(states):
+            raise LoopfuseError(_lib.LF_EINVAL, "reserve: a session appears twice in one call")
         ids = self._ids([s.slot_id for s in states])
         cnt = self._ids(counts)
         start = torch.empty(len(states), dtype=torch.int32, device=self.device)
@@ -381,6 +383,23 @@ class KVPool:
         self._call("lf_pool_free", self._meta_ref(), ids.data_ptr(), len(states), self._stream())
         for s in states:
             s.current_len = 0
+
+    def adopt(self, keep: KVState, branch: KVState) -> None:
+        """``keep`` takes over ``branch``'s block-table row (a speculative branch that turned
+        out right): keep's own pages are dropped on the device, the handle is re-pointed at the
+        branch's row and length, and keep's old row returns to the free slots at the tail, as
+        ``release`` would return it.  ``branch`` is spent: use ``keep`` from now on."""
+        if keep.slot_id not in self._active or branch.slot_id not in self._active or \
+                keep.slot_id == branch.slot_id:
+            raise LoopfuseError(_lib.LF_EINVAL, "adopt: both sessions must be open and distinct")
+        self.free(keep)
+        old = keep.slot_id
+        del self._active[branch.slot_id]
+        del self._active[old]
+        keep.slot_id, keep.current_len = branch.slot_id, branch.current_len
+        branch.current_len = 0
+        self._active[keep.slot_id] = keep
+        self._free_slots.append(old)
 
     def release_all(self, states: Sequence[KVState]) -> None:
         """Batched ``release``: one device free for all, slots back in the given order."""

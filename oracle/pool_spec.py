@@ -26,7 +26,9 @@ initially ``0, 1, ..., P-1``.
     ceil(len/16)`` pages are popped from the queue head and appended to its
     block table with refcount 1; ``len += n``.  All or nothing: if the total
     need exceeds the free count (ENOPAGES) or any session would pass
-    ``max_pages_per_seq`` pages (EOVERFLOW), nothing changes.
+    ``max_pages_per_seq`` pages (EOVERFLOW), nothing changes.  The sessions
+    must be distinct and the counts non-negative (EINVAL); the first offending
+    entry in call order decides between EINVAL and EOVERFLOW.
 ``fork(src, dsts, prefix_len)``
     Each destination (empty) gets the source's first ``prefix_len // 16`` page
     ids (shared; refcount += 1 per destination).  If ``prefix_len % 16`` is
@@ -163,9 +165,11 @@ class PagedKVPoolSpec:
     def reserve(self, seqs: Sequence[int], n_new: Sequence[int]) -> List[int]:
         """Returns each session's start position; raises PoolError on failure."""
         needs = []
+        seen = set()
         for s, n in zip(seqs, n_new):
-            if n < 0:
-                raise PoolError(EINVAL, "negative token count")
+            if n < 0 or s in seen:
+                raise PoolError(EINVAL, "negative token count or repeated session")
+            seen.add(s)
             old = self.pages_for(self.seq_len[s])
             new = self.pages_for(self.seq_len[s] + n)
             if new > self.max_pages_per_seq:

@@ -1,8 +1,8 @@
 """Generate the golden fixtures in this folder from the reference's own code.
 
-Run once, in a checkout that has the reference next to it:
+Run once, giving the path of a checkout of the reference (required):
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <path to the loopfuse checkout>
 
 The reference is a flat Python package (its root directory *is* the
 ``loopfuse`` package), so it is imported through a temporary directory holding
@@ -17,6 +17,10 @@ kvpool_trace.json      a scripted session on ``loopfuse.runtime.kv_pool.KVPool``
 phase_select.json      ``PhaseSelectPass`` annotations of the 3-step GPT-2
                        program (``tests/conftest.py:23-30`` of the reference)
                        for every ``KernelTarget``, plus IR byte arithmetic.
+passes.json            ``SpecPrefillPass`` insertions and annotations on programs
+                       with varied tool names and latencies (run twice, for
+                       idempotence), ``PassManager.run_until_fixed_point`` result
+                       flags, and ``RooflineAnalyzer(A100_SPEC)`` reports.
 attention_fp16.npz     seeded MHA fp16 inputs and the reference's own checks:
                        ``_reference_decode_attn`` (``kernels/triton/
                        decode_attn.py:178-184``) and the fp32 SDPA causal
@@ -122,6 +126,61 @@ def phase_select():
     return out
 
 
+def _pass_programs():
+    """(name, builder calls) of the programs the pass fixtures cover."""
+    return [
+        ("react3", [(0, "search", 150.0, True), (1, "lookup", 80.0, False), (2, None, 0.0, False)]),
+        ("tools", [(0, "execute_code", 120.0, True), (1, "run_shell", 500.0, False),
+                   (2, "web_search", 25.0, False), (3, "calculator", 40.0, False),
+                   (4, "lookup_db", 18.0, False), (5, "search", 300.0, False)]),
+        ("long", [(i, "search" if i % 2 else "fetch", 60.0 + 10 * i, i == 0) for i in range(12)]),
+    ]
+
+
+def _build(mod_builder, cfg, kv, steps, target):
+    b = mod_builder.AgentProgramBuilder("p", cfg, kv)
+    for sid, tool, lat, first in steps:
+        b.add_react_step(sid, tool, lat, is_first_step=first)
+    return b.set_target(target).build()
+
+
+def passes():
+    import loopfuse.ir.builder as builder
+    from loopfuse.ir.dialect import GPT2_CONFIG, GPT2_KV_CONFIG, KernelTarget, SpeculativePrefillOp
+    from loopfuse.passes.base import PassManager
+    from loopfuse.passes.phase_select import PhaseSelectPass
+    from loopfuse.passes.spec_prefill import SpecPrefillPass
+    from loopfuse.analysis.roofline import A100_SPEC, RooflineAnalyzer
+    out = {}
+    for name, steps in _pass_programs():
+        prog = _build(builder, GPT2_CONFIG, GPT2_KV_CONFIG, steps, KernelTarget.CUDA)
+        p = SpecPrefillPass()
+        r1, r2 = p.run(prog), p.run(prog)
+        layout = [[[type(o).__name__ for o in reg]
+                   for reg in (s.observe_region, s.reason_region, s.act_region)]
+                  for s in prog.steps]
+        spec_md = [{k: op.metadata[k] for k in ("confidence", "available_window_ms")}
+                   for op in prog.ops_by_type(SpeculativePrefillOp)]
+        fresh = _build(builder, GPT2_CONFIG, GPT2_KV_CONFIG, steps, KernelTarget.CUDA)
+        fp = PassManager([SpecPrefillPass(), PhaseSelectPass()]).run_until_fixed_point(fresh, 4)
+        roof = RooflineAnalyzer(A100_SPEC).analyze_program(
+            _build(builder, GPT2_CONFIG, GPT2_KV_CONFIG, steps, KernelTarget.CUDA))
+        out[name] = {
+            "spec_first": {"changed": r1.changed, "annotations": r1.annotations},
+            "spec_second": {"changed": r2.changed, "annotations": r2.annotations},
+            "layout": layout, "spec_metadata": spec_md,
+            "fixed_point": [[r.pass_name, r.changed] for r in fp],
+            "roofline": {"points": [[pt.op_name, pt.phase.value if pt.phase else None, pt.flops,
+                                     pt.bytes_accessed, pt.is_compute_bound,
+                                     pt.achieved_efficiency, pt.bottleneck]
+                                    for pt in roof.op_points],
+                         "phase_summary": roof.phase_summary, "total_flops": roof.total_flops,
+                         "total_bytes": roof.total_bytes, "gpu_idle_ms": roof.gpu_idle_ms,
+                         "text": roof.phase_breakdown_str()},
+        }
+    return out
+
+
 def attention_fp16():
     from loopfuse.kernels.triton.decode_attn import _reference_decode_attn
     import torch.nn.functional as F
@@ -142,12 +201,15 @@ def attention_fp16():
 
 
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
-    _import_reference(ref)
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path to the loopfuse checkout>")
+    _import_reference(sys.argv[1])
     with open(os.path.join(HERE, "kvpool_trace.json"), "w") as f:
         json.dump(kvpool_trace(), f, indent=1)
     with open(os.path.join(HERE, "phase_select.json"), "w") as f:
         json.dump(phase_select(), f, indent=1)
+    with open(os.path.join(HERE, "passes.json"), "w") as f:
+        json.dump(passes(), f, indent=1)
     np.savez_compressed(os.path.join(HERE, "attention_fp16.npz"), **attention_fp16())
     print("golden fixtures written to", HERE)
 

@@ -6,7 +6,7 @@ import random
 import pytest
 import torch
 
-from oracle.pool_spec import ENOPAGES, EOVERFLOW, PAGE, PagedKVPoolSpec, PoolError, page_hash
+from oracle.pool_spec import EINVAL, ENOPAGES, EOVERFLOW, PAGE, PagedKVPoolSpec, PoolError, page_hash
 
 
 def test_reference_slot_trace(golden_dir):
@@ -164,3 +164,22 @@ def test_dedup_registry_capacity_and_order():
     tail = sp.free_queue[q0:]
     assert tail == sorted(tail) and len(tail) == 4
     _check_invariants(sp)
+
+
+def test_reserve_rejects_a_repeated_session_without_side_effects():
+    sp = PagedKVPoolSpec(num_pages=16, max_seqs=4, max_pages_per_seq=8)
+    a, b = sp.open_seq(), sp.open_seq()
+    sp.reserve([a], [20])
+    before = sp.snapshot()
+    for seqs, counts in (([a, b, a], [1, 2, 3]), ([b, b], [16, 16])):
+        try:
+            sp.reserve(seqs, counts)
+            raise AssertionError("a repeated session must be rejected")
+        except PoolError as e:
+            assert e.code == EINVAL
+        assert sp.snapshot() == before
+    # the first offending entry in call order decides: an overflow before the repeat wins
+    try:
+        sp.reserve([b, a, a], [8 * 16 + 1, 1, 1])
+    except PoolError as e:
+        assert e.code == EOVERFLOW
