@@ -221,8 +221,9 @@ int lf_pool_clear_status(const lf_pool_meta* m, void* stream);
 
 /* Allocation step of append: session seq_ids[i] grows by n_new[i] tokens,
  * taking ceil-page deltas from the queue head in order; start_pos[i] receives
- * its old length.  All or nothing.  seq_ids must be distinct: a repeated id
- * is rejected with LF_EINVAL in the sticky status (nothing changes). */
+ * its old length.  All or nothing.  A session that grows (n_new > 0) must
+ * appear once; zero-count entries (padding rows) may repeat.  A conflicting
+ * entry is rejected with LF_EINVAL in the sticky status (nothing changes). */
 int lf_pool_reserve(const lf_pool_meta* m, const int32_t* seq_ids, const int32_t* n_new, int n,
                     int32_t* start_pos, void* stream);
 

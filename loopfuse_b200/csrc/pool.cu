@@ -46,18 +46,27 @@ reserve_kernel(Meta m, const int32_t* __restrict__ seq_ids, const int32_t* __res
     __shared__ int buf[32];
     __shared__ unsigned seen[kDupBits / 32];
     if (status_of(m) != LF_OK) return;
-    // Every session may appear once: the page deltas are computed from each session's length
-    // before the call, so a repeated id would take pages twice.  A bitmap finds whether any id
-    // repeats; only then does the exact scan name the first repeat in call order.
+    // A session that grows appears once: the page deltas are computed from each session's
+    // length before the call, so a repeated id would take pages twice (and its entries would
+    // race on its length).  Entries of zero tokens change nothing and may repeat -- padding rows
+    // of a fixed-size batch -- unless their session also grows in this call.  A bitmap of the
+    // growing sessions finds whether any entry conflicts; only then does the exact scan name
+    // the first conflicting entry in call order.
     int dup = 0;
     if (m.S <= kDupBits) {
         for (int w = threadIdx.x; w < (m.S + 31) / 32; w += kMetaThreads) seen[w] = 0u;
         __syncthreads();
         for (int i = threadIdx.x; i < n; i += kMetaThreads) {
             const int s = seq_ids[i];
-            if (s < 0 || s >= m.S) continue;
+            if (s < 0 || s >= m.S || n_new[i] == 0) continue;
             const unsigned bit = 1u << (s & 31);
             if (atomicOr(&seen[s >> 5], bit) & bit) dup = 1;
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < n; i += kMetaThreads) {
+            const int s = seq_ids[i];
+            if (s < 0 || s >= m.S || n_new[i] != 0) continue;
+            if (seen[s >> 5] & (1u << (s & 31))) dup = 1;
         }
         dup = -block_min(-dup, buf);
     } else {
@@ -70,7 +79,8 @@ reserve_kernel(Meta m, const int32_t* __restrict__ seq_ids, const int32_t* __res
         const int t = n_new[i];
         bool repeat = false;
         if (dup)
-            for (int j = 0; j < i && !repeat; ++j) repeat = seq_ids[j] == s;
+            for (int j = 0; j < i && !repeat; ++j)
+                repeat = seq_ids[j] == s && (t != 0 || n_new[j] != 0);
         if (s < 0 || s >= m.S || t < 0 || repeat) {
             first_bad = min(first_bad, i * 8 + LF_EINVAL);
             continue;

@@ -71,6 +71,9 @@ class StepStats:
     bytes_read_unshared: int
     bytes_written: int
     launches: int
+    prefill_ms: float = 0.0          # tool-output append + paged prefill, all layers
+    decode_ms: float = 0.0           # the decode iterations
+    decode_bytes_read: int = 0       # bytes_read of the decode iterations alone
 
 
 @dataclass
@@ -163,10 +166,13 @@ class FusionLoop:
             kp, vp = pool.layer_pages(layer)
             att.prefill_paged(self.qbuf[:total], kp, vp, table, cu, lens, max(T))
             launches += 2
+        ev_mid = torch.cuda.Event(enable_timing=True)
+        ev_mid.record()
         ctx = [s.current_len for s in S]
         pre_pages = sum(self._pages(L) for L in ctx)
         bytes_read += c.layers * pre_pages * self.page_bytes
         bytes_unshared += c.layers * pre_pages * self.page_bytes
+        prefill_bytes = bytes_read
         if self.spec is not None:
             self.spec.reserve([s.slot_id for s in S], T)
             self._check()
@@ -215,7 +221,8 @@ class FusionLoop:
             pool._raise_if_failed("fusion-loop decode")
         written = c.layers * (total + c.decode_tokens * len(S)) * 2 * c.kv_heads * c.head_dim * 2
         return StepStats(step, total, ev0.elapsed_time(ev1), bytes_read, bytes_unshared, written,
-                         launches)
+                         launches, ev0.elapsed_time(ev_mid), ev_mid.elapsed_time(ev1),
+                         bytes_read - prefill_bytes)
 
     def _capture_decode(self, S, dec_idx) -> dict:
         """One decode iteration of every session as a CUDA graph: pool reserve and block-table

@@ -6,6 +6,7 @@
     python -m loopfuse_b200.profile_cases paged [--sessions 128] [--reps 3]
     python -m loopfuse_b200.profile_cases epilogue [--tokens 16384] [--reps 3]
     python -m loopfuse_b200.profile_cases dedup [--sessions 512] [--reps 3]
+    python -m loopfuse_b200.profile_cases fusion_decode [--sessions 64] [--private 600] [--reps 3]
 
 Each case builds its inputs, runs one warm-up launch and then ``--reps`` launches of the op,
 so a capture can skip the warm-up (``-s``) and take one to three launches (``-c``).  The decode
@@ -37,6 +38,55 @@ def run_decode(sessions: int, reps: int, pps: int) -> None:
     b = decode_bytes(w)
     print(f"decode sessions={sessions} pages_per_split={pps} unique_bytes={b['unique']} "
           f"suffix_kv_bytes={b['suffix_kv']}")
+
+
+def run_fusion_decode(sessions: int, reps: int, pps: int, private: int, layers: int = 4) -> None:
+    """One decode call of the KV-fusion loop's shape: ``sessions`` sessions sharing a 4096-token
+    prefix, each with about ``private`` tokens of its own (uniform in [private/2, 3private/2]),
+    Llama-3-8B attention shapes.  ``layers`` independent pools are cycled, as the loop's layers
+    are, so successive calls do not find their pages in L2.  Prints the CUDA-event time per call
+    and the algorithmic bytes."""
+    g = torch.Generator().manual_seed(3)
+    lens = [4096 + int(x) for x in torch.randint(private // 2, 3 * private // 2 + 1, (sessions,),
+                                                 generator=g)]
+    ws_ = [decode_inputs(N=sessions, lengths=lens, prefix_tokens=4096, seed=l) for l in range(layers)]
+    w0 = ws_[0]
+    max_pages = w0.block_table.shape[1]
+    pps = pps or att.default_pages_per_split(sessions, 8, max_pages, w0.n_prefix_pages)
+    out = torch.empty_like(w0.q)
+    ws = torch.empty(att.decode_workspace_bytes(sessions, 32, 128, max_pages, pps, w0.n_prefix_pages),
+                     dtype=torch.uint8, device="cuda")
+
+    def call(w):
+        att.paged_decode(w.q, w.k_pages, w.v_pages, w.block_table, w.seq_lens,
+                         num_prefix_pages=w.n_prefix_pages, pages_per_split=pps, out=out, workspace=ws)
+    for w in ws_:
+        call(w)
+    torch.cuda.synchronize()
+    # The loop replays its decode calls from a CUDA graph; so does this case (host launch cost
+    # would otherwise exceed the GPU time of a call).
+    per_graph = 8 * layers
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph):
+            for i in range(per_graph):
+                call(ws_[i % layers])
+    torch.cuda.current_stream().wait_stream(side)
+    graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(max(1, reps)):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / (max(1, reps) * per_graph)
+    b = decode_bytes(w0)
+    print(f"fusion decode sessions={sessions} private~{private} pages_per_split={pps} "
+          f"unique_bytes={b['unique']} suffix_kv_bytes={b['suffix_kv']} ms_per_call={ms:.4f} "
+          f"GBps={b['unique'] / ms / 1e6:.1f}")
 
 
 def run_prefill(batch: int, seq: int, reps: int) -> None:
@@ -139,7 +189,9 @@ def run_dedup(sessions: int, reps: int) -> None:
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["decode", "prefill", "pool", "paged", "epilogue", "dedup"])
+    ap.add_argument("case", choices=["decode", "prefill", "pool", "paged", "epilogue", "dedup",
+                                     "fusion_decode"])
+    ap.add_argument("--private", type=int, default=600)
     ap.add_argument("--sessions", type=int, default=32)
     ap.add_argument("--batch", type=int, default=2)
     ap.add_argument("--seq", type=int, default=4096)
@@ -150,6 +202,8 @@ def main(argv=None) -> None:
     torch.cuda.set_device(0)
     if a.case == "decode":
         run_decode(a.sessions, a.reps, a.pages_per_split)
+    elif a.case == "fusion_decode":
+        run_fusion_decode(a.sessions, a.reps, a.pages_per_split, a.private)
     elif a.case == "prefill":
         run_prefill(a.batch, a.seq, a.reps)
     elif a.case == "paged":

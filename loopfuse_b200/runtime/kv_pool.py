@@ -254,8 +254,12 @@ class KVPool:
             if s.current_len + n > self.max_seq_len:
                 raise RuntimeError(f"KV cache overflow: current_len={s.current_len} + "
                                    f"seq_new={n} > max_seq_len={self.max_seq_len}")
-        if len({s.slot_id for s in states}) != len(states):
-            raise LoopfuseError(_lib.LF_EINVAL, "reserve: a session appears twice in one call")
+        grows = {}
+        for s, n in zip(states, counts):
+            if s.slot_id in grows and (n != 0 or grows[s.slot_id]):
+                raise LoopfuseError(_lib.LF_EINVAL, "reserve: a growing session appears twice "
+                                                    "in one call")
+            grows[s.slot_id] = grows.get(s.slot_id, False) or n != 0
         ids = self._ids([s.slot_id for s in states])
         cnt = self._ids(counts)
         start = torch.empty(len(states), dtype=torch.int32, device=self.device)

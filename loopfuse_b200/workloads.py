@@ -77,12 +77,16 @@ def decode_lengths(n: int, lmin: int, lmax: int, seed: int) -> List[int]:
 
 def decode_inputs(N: int = 256, Hq: int = 32, Hkv: int = 8, D: int = 128, lmin: int = 1024,
                   lmax: int = 32768, prefix_tokens: int = 2048, seed: int = 0, device="cuda",
-                  lengths: Optional[List[int]] = None, pool_factor: float = 1.1) -> DecodeWorkload:
+                  lengths: Optional[List[int]] = None, pool_factor: float = 1.1,
+                  table_seed: Optional[int] = None) -> DecodeWorkload:
+    """``seed`` draws the lengths (unless given), the page permutation (unless ``table_seed``
+    is given: then the block table is that seed's, shared by every caller using it) and the
+    q / K / V values."""
     lengths = lengths if lengths is not None else decode_lengths(N, lmin, lmax, seed)
     n_pre = prefix_tokens // PAGE
     own = [max(0, math.ceil(L / PAGE) - n_pre) for L in lengths]
     P = math.ceil(pool_factor * (n_pre + sum(own)))
-    gcpu = torch.Generator().manual_seed(seed + 1)
+    gcpu = torch.Generator().manual_seed((seed if table_seed is None else table_seed) + 1)
     perm = torch.randperm(P, generator=gcpu).tolist()
     prefix = perm[:n_pre]
     max_pages = max(math.ceil(L / PAGE) for L in lengths)
@@ -117,14 +121,21 @@ def decode_bytes(w: DecodeWorkload, shared_prefix: bool = True) -> dict:
     prefix sharing must move).
     """
     N, Hq, D = w.q.shape
-    Hkv = w.k_pages.shape[1]
-    page_bytes = 2 * Hkv * PAGE * D * w.k_pages.element_size()       # K + V, all heads
-    n_pre = w.n_prefix_pages
-    pages_own = sum(max(0, math.ceil(L / PAGE) - n_pre) for L in w.lengths)
-    pages_pre_used = max((min(math.ceil(L / PAGE), n_pre) for L in w.lengths), default=0)
-    pages_logical = sum(math.ceil(L / PAGE) for L in w.lengths)
+    return decode_bytes_from_lengths(w.lengths, Hq, w.k_pages.shape[1], D, w.n_prefix_pages,
+                                     w.k_pages.element_size())
+
+
+def decode_bytes_from_lengths(lengths: List[int], Hq: int, Hkv: int, D: int, n_pre: int,
+                              elem: int = 2) -> dict:
+    """``decode_bytes`` from the session lengths alone (no device tensors needed)."""
+    N = len(lengths)
+    page_bytes = 2 * Hkv * PAGE * D * elem                            # K + V, all heads
+    pages_own = sum(max(0, math.ceil(L / PAGE) - n_pre) for L in lengths)
+    pages_pre_used = max((min(math.ceil(L / PAGE), n_pre) for L in lengths), default=0)
+    pages_logical = sum(math.ceil(L / PAGE) for L in lengths)
     small = 2 * N * Hq * D * 2 + 4 * N + 4 * pages_logical
     return {"unique": (pages_pre_used + pages_own) * page_bytes + small,
             "logical": pages_logical * page_bytes + small,
             "suffix_kv": pages_own * page_bytes,
-            "page_bytes": page_bytes}
+            "page_bytes": page_bytes,
+            "pool_pages": math.ceil(1.1 * (n_pre + pages_own))}

@@ -26,9 +26,12 @@ initially ``0, 1, ..., P-1``.
     ceil(len/16)`` pages are popped from the queue head and appended to its
     block table with refcount 1; ``len += n``.  All or nothing: if the total
     need exceeds the free count (ENOPAGES) or any session would pass
-    ``max_pages_per_seq`` pages (EOVERFLOW), nothing changes.  The sessions
-    must be distinct and the counts non-negative (EINVAL); the first offending
-    entry in call order decides between EINVAL and EOVERFLOW.
+    ``max_pages_per_seq`` pages (EOVERFLOW), nothing changes.  Counts must be
+    non-negative and a session that grows must appear once: an entry is
+    EINVAL when an earlier entry names the same session and either of the two
+    counts is non-zero (zero-count entries, e.g. padding rows, may repeat).
+    The first offending entry in call order decides between EINVAL and
+    EOVERFLOW.
 ``fork(src, dsts, prefix_len)``
     Each destination (empty) gets the source's first ``prefix_len // 16`` page
     ids (shared; refcount += 1 per destination).  If ``prefix_len % 16`` is
@@ -165,11 +168,11 @@ class PagedKVPoolSpec:
     def reserve(self, seqs: Sequence[int], n_new: Sequence[int]) -> List[int]:
         """Returns each session's start position; raises PoolError on failure."""
         needs = []
-        seen = set()
+        grows = {}                                  # session -> an earlier entry adds tokens
         for s, n in zip(seqs, n_new):
-            if n < 0 or s in seen:
-                raise PoolError(EINVAL, "negative token count or repeated session")
-            seen.add(s)
+            if n < 0 or (s in grows and (n != 0 or grows[s])):
+                raise PoolError(EINVAL, "negative token count or repeated growing session")
+            grows[s] = grows.get(s, False) or n != 0
             old = self.pages_for(self.seq_len[s])
             new = self.pages_for(self.seq_len[s] + n)
             if new > self.max_pages_per_seq:

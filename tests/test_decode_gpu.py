@@ -71,15 +71,19 @@ def test_decode_reference_api_matches_reference_check():
     _check(o, ref)
 
 
-def test_decode_full_size_sampled():
-    """The 256-session, 2048-token-prefix workload at full size: sampled sessions vs the oracle,
-    and the shared-prefix path equal to the per-session path on every session."""
+def test_decode_full_size_every_session():
+    """The 256-session, 2048-token-prefix workload at full size: every session against an fp32
+    attention computed on the GPU, sampled sessions against the CPU oracle, and the
+    shared-prefix path equal to the per-session path on every session."""
+    from fp32_gpu_reference import decode_errors
     w = decode_inputs(seed=0)
     o_sh = att.paged_decode(w.q, w.k_pages, w.v_pages, w.block_table, w.seq_lens,
                             num_prefix_pages=w.n_prefix_pages)
     o_ns = att.paged_decode(w.q, w.k_pages, w.v_pages, w.block_table, w.seq_lens)
     d = (o_sh.float() - o_ns.float()).abs()
     assert d.max().item() <= TOL_MAX and d.mean().item() <= TOL_MEAN
+    mx, mean, n = decode_errors(w.q, w.k_pages, w.v_pages, w.block_table, w.lengths, o_sh)
+    assert n == 256 and mx <= TOL_MAX and mean <= TOL_MEAN, (mx, mean)
     order = sorted(range(w.num_seqs), key=lambda i: w.lengths[i])
     idx = [order[0], order[1], order[len(order) // 2], order[-1]]
     ref, _ = _oracle(w, idx)

@@ -170,3 +170,79 @@ def test_oversubscribed_pool_reports_exhaustion_without_side_effects():
         pool.write(b, torch.cat([k, k], 2), torch.cat([k, k], 2))
     after = pool.snapshot()
     assert after == before
+
+
+def _raw_meta_args(pool):
+    return pool._meta_ref(), torch.cuda.current_stream().cuda_stream
+
+
+def test_reserve_with_a_repeated_session_is_rejected_like_the_spec():
+    """The host API refuses a repeated session; the device kernel, called directly, reports
+    LF_EINVAL through the sticky status and changes nothing -- the spec's answer."""
+    from loopfuse_b200 import _lib
+    from loopfuse_b200._lib import LoopfuseError
+    pool = KVPool(num_layers=1, num_heads=2, head_dim=64, max_seq_len=128, max_slots=3,
+                  dtype=torch.bfloat16, num_pages=16)
+    spec = PagedKVPoolSpec(num_pages=16, max_seqs=3, max_pages_per_seq=8)
+    a, b = pool.alloc(), pool.alloc()
+    spec.open_seq(), spec.open_seq()
+    pool.reserve([a], [20])
+    spec.reserve([a.slot_id], [20])
+    _same(pool, spec)
+    with pytest.raises(LoopfuseError):
+        pool.reserve([a, b, a], [1, 1, 1])
+    ids = torch.tensor([b.slot_id, a.slot_id, b.slot_id], dtype=torch.int32, device="cuda")
+    cnt = torch.tensor([16, 16, 16], dtype=torch.int32, device="cuda")
+    start = torch.empty(3, dtype=torch.int32, device="cuda")
+    meta, st = _raw_meta_args(pool)
+    assert _lib.lib().lf_pool_reserve(meta, ids.data_ptr(), cnt.data_ptr(), 3, start.data_ptr(),
+                                      st) == _lib.LF_OK
+    with pytest.raises(PoolError) as e:
+        spec.reserve([b.slot_id, a.slot_id, b.slot_id], [16, 16, 16])
+    assert pool.status() == e.value.code == _lib.LF_EINVAL
+    _lib.call("lf_pool_clear_status", meta, st)
+    _same(pool, spec)
+    # zero-count rows (a fixed-size batch's padding) may repeat a session that does not grow
+    assert pool.reserve([b, a, b, b], [0, 5, 0, 0]).tolist() == \
+        spec.reserve([b.slot_id, a.slot_id, b.slot_id, b.slot_id], [0, 5, 0, 0])
+    _same(pool, spec)
+
+
+def test_write_to_a_position_without_a_page_sets_the_status_and_stores_nothing():
+    """A K/V row whose position has no reserved page (a stale start position) is skipped and
+    reported (LF_EINVAL in the sticky status) instead of being stored through page id -1; the
+    rows that do have pages are stored."""
+    from loopfuse_b200 import _lib
+    L, H, D = 2, 2, 64
+    pool = KVPool(num_layers=L, num_heads=H, head_dim=D, max_seq_len=64, max_slots=2,
+                  dtype=torch.bfloat16, num_pages=8)
+    a = pool.alloc()
+    pool.reserve([a], [16])                       # one page
+    keys_before = pool.keys.clone()
+    kv = torch.randn(L, 20, H, D, device="cuda").bfloat16()
+    ids = torch.tensor([a.slot_id], dtype=torch.int32, device="cuda")
+    start = torch.tensor([0], dtype=torch.int32, device="cuda")
+    cu = torch.tensor([0, 20], dtype=torch.int32, device="cuda")      # rows 16..19 have no page
+    meta, st = _raw_meta_args(pool)
+    rc = _lib.lib().lf_pool_write_kv(meta, ids.data_ptr(), start.data_ptr(), cu.data_ptr(), 1, 20,
+                                     kv.data_ptr(), kv.data_ptr(), kv.stride(0), kv.stride(1),
+                                     kv.stride(2), pool.keys.data_ptr(), pool.values.data_ptr(), L,
+                                     H, D, st)
+    assert rc == _lib.LF_OK
+    assert pool.status() == _lib.LF_EINVAL
+    page = pool.snapshot()["block_table"][a.slot_id][0]
+    for l in range(L):
+        assert torch.equal(pool.keys[l, page].permute(1, 0, 2), kv[l, :16])
+    other = [p for p in range(pool.num_pages) if p != page]
+    assert torch.equal(pool.keys[:, other], keys_before[:, other])
+    _lib.call("lf_pool_clear_status", meta, st)
+    # a stale start position past the session's pages is skipped the same way
+    start.fill_(40)
+    cu[1] = 4
+    rc = _lib.lib().lf_pool_write_kv(meta, ids.data_ptr(), start.data_ptr(), cu.data_ptr(), 1, 4,
+                                     kv.data_ptr(), kv.data_ptr(), kv.stride(0), kv.stride(1),
+                                     kv.stride(2), pool.keys.data_ptr(), pool.values.data_ptr(), L,
+                                     H, D, st)
+    assert rc == _lib.LF_OK and pool.status() == _lib.LF_EINVAL
+    assert torch.equal(pool.keys[:, other], keys_before[:, other])
+    _lib.call("lf_pool_clear_status", meta, st)

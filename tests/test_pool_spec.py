@@ -183,3 +183,11 @@ def test_reserve_rejects_a_repeated_session_without_side_effects():
         sp.reserve([b, a, a], [8 * 16 + 1, 1, 1])
     except PoolError as e:
         assert e.code == EOVERFLOW
+    # zero-count entries (padding rows) may repeat, unless their session also grows
+    assert sp.reserve([b, a, b, b], [0, 3, 0, 0]) == [0, 20, 0, 0]
+    for seqs, counts in (([a, b, a], [0, 1, 2]), ([a, b, a], [2, 1, 0])):
+        try:
+            sp.reserve(seqs, counts)
+            raise AssertionError("a growing session must appear once")
+        except PoolError as e:
+            assert e.code == EINVAL
