@@ -297,7 +297,7 @@ def agent_measure(args, grp) -> dict:
     loop.setup()                     # system prompt prefill + fork source, decode graph capture
     torch.cuda.synchronize()
     grp.barrier()
-    st = loop.run()
+    st = loop.run(profile_ops=True)
     wall = grp.max(st.wall_s)
     steps = grp.sum(float(st.steps_done))
     res = {"metric": "agent steps/s", "value": round(steps / wall, 2), "unit": "steps/s",
@@ -314,7 +314,8 @@ def agent_measure(args, grp) -> dict:
                      "decode_s": round(st.decode_s, 3), "spec_s": round(st.spec_s, 3),
                      "model_tflops": round(model.flops_per_token() *
                                            (st.prefill_tokens + st.decode_tokens) /
-                                           st.gpu_busy_s / 1e12, 1) if st.gpu_busy_s else None}}
+                                           st.gpu_busy_s / 1e12, 1) if st.gpu_busy_s else None,
+                     "kernels": st.kernels}}
     del loop, model
     torch.cuda.empty_cache()
     return res

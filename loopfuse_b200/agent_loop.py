@@ -99,9 +99,13 @@ class AgentLoopStats:
     decode_s: float = 0.0
     spec_s: float = 0.0
     idle_waits: int = 0
+    kernels: Optional[dict] = None     # per-kernel-class attribution (run(profile_ops=True))
 
 
 class AgentLoop:
+    PROFILE_SESSIONS = 64        # sessions in the attributed prefill batch
+    PROFILE_PREFILL = 128        # new tokens per session in it (about one tool output)
+
     def __init__(self, model: LlamaShaped, cfg: AgentLoopConfig, session_ids: Optional[List[int]] = None,
                  device=None):
         self.model, self.cfg = model, cfg
@@ -117,9 +121,12 @@ class AgentLoop:
         n = len(self.ids)
         own = [cfg.question_tokens + int(self.tool_len[i].sum()) +
                cfg.steps * (cfg.decode_tokens + cfg.spec_tokens) for i in self.ids]
-        max_len = cfg.prefix_tokens + max(own) + 64
+        # slack past the longest session: the per-kernel attribution forwards after the loop
+        # append up to 2 decode tokens and one 128-token prefill chunk to a session
+        max_len = cfg.prefix_tokens + max(own) + 64 + 2 + self.PROFILE_PREFILL
         self.n_prefix_pages = cfg.prefix_tokens // PAGE
-        pages = self.n_prefix_pages + sum((o + PAGE - 1) // PAGE + 1 for o in own) + 16
+        pages = self.n_prefix_pages + sum((o + PAGE - 1) // PAGE + 1 for o in own) + 16 + \
+            n + min(n, self.PROFILE_SESSIONS) * (self.PROFILE_PREFILL // PAGE + 1)
         mc = model.cfg
         self.pool = KVPool(num_layers=mc.layers, num_heads=mc.q_heads, num_kv_heads=mc.kv_heads,
                            head_dim=mc.head_dim, max_seq_len=max_len, max_slots=n + 2,
@@ -164,7 +171,79 @@ class AgentLoop:
         stats.gpu_busy_s += time.perf_counter() - t0
         return out
 
-    def run(self) -> AgentLoopStats:
+    # -- per-kernel attribution ------------------------------------------------------------------
+    def _op_work(self, T: int, n_out: int, attn_flops: float, attn_bytes: float) -> dict:
+        """Algorithmic (FLOPs, HBM bytes) per op class of one forward of ``T`` new tokens
+        (``n_out`` sessions' last positions go through the LM head), summed over the layers."""
+        c = self.model.cfg
+        d, f, V, L = c.d_model, c.ffn, c.vocab, c.layers
+        nq, nkv = c.q_heads * c.head_dim, c.kv_heads * c.head_dim
+        qkv = nq + 2 * nkv
+
+        def gemm(m, k, n):
+            return 2.0 * m * k * n, 2.0 * (k * n + m * k + m * n)
+        w = {"qkv_gemm": gemm(T, d, qkv), "o_gemm": gemm(T, nq, d),
+             "gate_up_gemm": gemm(T, d, 2 * f), "down_gemm": gemm(T, f, d)}
+        out = {k: (L * v[0], L * v[1]) for k, v in w.items()}
+        out["qkv_rope_append"] = (0.0, L * 2.0 * T * (qkv + nq + 2 * nkv))
+        out["attention"] = (attn_flops, attn_bytes)
+        out["add_rmsnorm"] = (0.0, L * 2 * 4.0 * T * d * 2)
+        out["swiglu"] = (0.0, L * 2.0 * T * 3 * f)
+        out["lm_head"] = gemm(n_out, d, V)
+        return out
+
+    def _profile_ops(self, sessions: List["_Sess"], decode_steps: int = 2) -> dict:
+        """Per-kernel-class time and roofline of one decode iteration over every session of this
+        rank and of one prefill batch (``PROFILE_PREFILL`` new tokens for each of up to
+        ``PROFILE_SESSIONS`` sessions, about one tool output each), both at the sessions' final
+        lengths.  Eager forwards timed op by op with CUDA events; the stream is held by a
+        device-side spin while the host enqueues, so host gaps are not charged."""
+        from .analysis import kernel_roofline
+        from .llama import OpTimer
+        c, pool = self.model.cfg, self.pool
+        kv_tok = 2 * c.kv_heads * c.head_dim * 2 * c.layers           # K+V bytes per token
+        res = {}
+        for phase in ("decode", "prefill"):
+            chosen = sessions if phase == "decode" else sessions[:self.PROFILE_SESSIONS]
+            states = [s.state for s in chosen]
+            n = len(states)
+            per = 1 if phase == "decode" else self.PROFILE_PREFILL
+            reps = decode_steps if phase == "decode" else 1
+            acc: dict = {}
+            ctx = [st.current_len for st in states]
+            for _ in range(reps):
+                timer = OpTimer()
+                toks = torch.randint(0, self.vocab, (n * per,), device=self.device)
+                torch.cuda.synchronize(self.device)
+                timer.start(hold_cycles=200_000_000)
+                self.model.forward(toks, pool, states, [per] * n, n_prefix_pages=self.n_prefix_pages,
+                                   timer=timer)
+                torch.cuda.synchronize(self.device)
+                for k, v in timer.totals().items():
+                    acc[k] = acc.get(k, 0.0) + v / reps
+            pre = self.n_prefix_pages * PAGE
+            if phase == "decode":
+                own = sum(max(0, L + 1 - pre) for L in ctx)
+                a_bytes = float(kv_tok * (own + min(pre, max(ctx) + 1)))
+                a_flops = 4.0 * c.q_heads * c.head_dim * c.layers * sum(L + 1 for L in ctx)
+            else:
+                a_bytes = float(kv_tok * (sum(max(0, L + per - pre) for L in ctx) + pre))
+                pairs = sum(per * L + per * (per + 1) / 2 for L in ctx)
+                a_flops = 4.0 * c.q_heads * c.head_dim * c.layers * pairs
+            work = self._op_work(n * per, n, a_flops, a_bytes)
+            total = sum(acc.values())
+            ops = []
+            for k, ms in sorted(acc.items(), key=lambda kv: -kv[1]):
+                fl, by = work.get(k, (0.0, 0.0))
+                r = kernel_roofline(k, fl, by, ms * 1e-3) if (fl or by) else {"kernel": k}
+                r["ms"] = round(ms, 4)
+                r["share"] = round(ms / total, 4) if total else None
+                ops.append(r)
+            res[phase] = {"sessions": n, "new_tokens": n * per, "ms": round(total, 3),
+                          "mean_context": round(sum(ctx) / max(1, n), 1), "ops": ops}
+        return res
+
+    def run(self, profile_ops: bool = False) -> AgentLoopStats:
         cfg, pool = self.cfg, self.pool
         if self.root is None:
             self.setup()
@@ -250,5 +329,7 @@ class AgentLoop:
         torch.cuda.synchronize(self.device)
         stats.wall_s = time.perf_counter() - t_start
         stats.steps_per_s = stats.steps_done / stats.wall_s
+        if profile_ops:                       # after the timed loop, on its final state
+            stats.kernels = self._profile_ops(sessions)
         pool.release_all(states)
         return stats

@@ -1,22 +1,20 @@
-// Paged split-KV decode attention for sm_100a.
+// Paged split-KV decode attention for sm_100a: entry points, the combine kernel and the
+// launch sequence.
 //
 // Replaces the reference's decode_attention_fwd (kernels/triton/decode_attn.py:133-171,
 // one program per (batch, head) over a contiguous cache) and the non-compiling
 // ring_kv_decode_kernel (kernels/cuda/ring_kv_cache.cu:120-248).
 //
-// Work split.  CTA (split, kv_head, session) owns pages_per_split consecutive pages of one
-// session's block-table row and the Hq/Hkv query heads that share kv_head (GQA): every K/V
-// byte is read once for the whole group.  Four warps take the CTA's pages round-robin.
-// A page of one head is 16 rows x D bf16 = 4 KB contiguous; a warp reads it with 16-byte
-// loads, D/8 lanes per row, so each load instruction covers whole, adjacent rows.
-//
-// Per page a lane holds 8 dims of TPI tokens per instruction row.  q.k partial sums are
-// reduced over the D/8 lanes of a row with a reduce-scatter (each halving step exchanges
-// half of the group's heads), so a lane ends with the full score of one (token, head).
-// Online softmax runs in the log2 domain (q pre-scaled by scale*log2 e).  The warp's
-// running (max, sum, acc) are merged across warps through shared memory, and the CTA
-// writes one unnormalised partial (o, max, sum) per query head.  The combine kernel
-// merges a session's partials by log-sum-exp.
+// A decode is up to three launches on the caller's stream:
+//   split    CTA (split, kv_head, session) applies pages_per_split consecutive pages of the
+//            session's own block-table row to the Hq/Hkv query heads of kv_head (GQA: every K/V
+//            byte is read once for the whole group) and writes one unnormalised partial
+//            (o, max, sum) per query head.  Warp-level tensor-core kernel (decode_mma.cu).
+//   prefix   when the first num_prefix_pages table entries are a prefix shared by every
+//            session, those pages are applied once per group of sessions (tcgen05 kernel in
+//            prefill.cu for head_dim 128, decode_prefix.cu for 64), on a side stream forked
+//            next to the split launch; its partials go to their own slots.
+//   combine  one warp per (session, query head) merges the row's partials by log-sum-exp.
 #include "decode_common.cuh"
 
 #include <math.h>
@@ -26,151 +24,9 @@
 namespace lf {
 namespace decode {
 
-// part_o: [N, Hq, n_slots, D] fp32 (unnormalised); part_ml: [N, Hq, n_slots] (max, sum),
-// max in log2 units of the scaled scores.
-template <int D, int G>
-__global__ void __launch_bounds__(kThreads)
-split_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kp,
-             const uint16_t* __restrict__ vp, const int32_t* __restrict__ bt,
-             const int32_t* __restrict__ seq_lens, float* __restrict__ part_o,
-             float2* __restrict__ part_ml, int Hq, int Hkv, int num_pages, int max_pages,
-             int pages_per_split, int first_page, int n_slots, float qscale) {
-    using C = Cfg<D, G>;
-    const int split = blockIdx.x, h = blockIdx.y, n = blockIdx.z;
-    const int L = min(max(seq_lens[n], 0), max_pages * kPage);
-    const int npages = (L + kPage - 1) / kPage;
-    const int p_begin = first_page + split * pages_per_split;
-    if (p_begin >= npages) return;
-    const int p_end = min(p_begin + pages_per_split, npages);
+// Partial slots: part_o [N, Hq, n_slots, D] fp32 (unnormalised), part_ml [N, Hq, n_slots]
+// (max in log2 units of the scaled scores, sum).
 
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int c = lane % C::LPT;
-    const int sub = lane / C::LPT;
-    const int hl = head_of_chunk<D, G>(c);
-
-    float qf[G][8];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(q + ((size_t)n * Hq + h * G + g) * D + 8 * c);
-        unpack8(raw, qf[g]);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) qf[g][j] *= qscale;
-    }
-    float acc[G][8];
-#pragma unroll
-    for (int g = 0; g < G; ++g)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[g][j] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f;
-
-    const int32_t* bt_row = bt + (size_t)n * max_pages;
-    for (int pi = p_begin + warp; pi < p_end; pi += kWarps) {
-        const int page = checked_page(bt_row[pi], num_pages);
-        const size_t base = ((size_t)page * Hkv + h) * (size_t)(kPage * D);
-        const uint16_t* kb = kp + base + sub * D + 8 * c;
-        const uint16_t* vb = vp + base + sub * D + 8 * c;
-        uint4 kr[C::ROWS], vr[C::ROWS];
-#pragma unroll
-        for (int r = 0; r < C::ROWS; ++r) kr[r] = ldg_stream(kb + r * C::TPI * D);
-#pragma unroll
-        for (int r = 0; r < C::ROWS; ++r) vr[r] = ldg_stream(vb + r * C::TPI * D);
-
-        const int tok0 = pi * kPage + sub;
-        float s[C::ROWS];
-#pragma unroll
-        for (int r = 0; r < C::ROWS; ++r) {
-            float kf[8];
-            unpack8(kr[r], kf);
-            float part[G];
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-                float a = 0.f;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) a = fmaf(qf[g][j], kf[j], a);
-                part[g] = a;
-            }
-            const float sc = reduce_scatter_row<D, G>(part, c);
-            s[r] = (tok0 + r * C::TPI < L) ? sc : -INFINITY;
-        }
-        float mx = s[0];
-#pragma unroll
-        for (int r = 1; r < C::ROWS; ++r) mx = fmaxf(mx, s[r]);
-#pragma unroll
-        for (int off = C::LPT; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-        // Every page below npages holds at least one valid token, so m_new is finite.
-        const float m_new = fmaxf(m_run, mx);
-        const float alpha = fast_exp2(m_run - m_new);
-        float p[C::ROWS];
-        float ps = 0.f;
-#pragma unroll
-        for (int r = 0; r < C::ROWS; ++r) {
-            p[r] = fast_exp2(s[r] - m_new);
-            ps += p[r];
-        }
-#pragma unroll
-        for (int off = C::LPT; off < 32; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
-        l_run = l_run * alpha + ps;
-        m_run = m_new;
-
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-            const float ag = __shfl_sync(0xffffffffu, alpha, chunk_of_head<D, G>(g));
-#pragma unroll
-            for (int j = 0; j < 8; ++j) acc[g][j] *= ag;
-        }
-#pragma unroll
-        for (int r = 0; r < C::ROWS; ++r) {
-            float vf[8];
-            unpack8(vr[r], vf);
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const float pg = __shfl_sync(0xffffffffu, p[r], sub * C::LPT + chunk_of_head<D, G>(g));
-#pragma unroll
-                for (int j = 0; j < 8; ++j) acc[g][j] = fmaf(pg, vf[j], acc[g][j]);
-            }
-        }
-    }
-
-    // Sum the token-row sub-groups of the warp.
-#pragma unroll
-    for (int off = C::LPT; off < 32; off <<= 1)
-#pragma unroll
-        for (int g = 0; g < G; ++g)
-#pragma unroll
-            for (int j = 0; j < 8; ++j) acc[g][j] += __shfl_xor_sync(0xffffffffu, acc[g][j], off);
-
-    __shared__ float sm_m[kWarps][G], sm_l[kWarps][G];
-    __shared__ float sm_acc[kWarps][G][D];
-    if (sub == 0) {
-        if (c == chunk_of_head<D, G>(hl)) {
-            sm_m[warp][hl] = m_run;
-            sm_l[warp][hl] = l_run;
-        }
-#pragma unroll
-        for (int g = 0; g < G; ++g)
-#pragma unroll
-            for (int j = 0; j < 8; ++j) sm_acc[warp][g][8 * c + j] = acc[g][j];
-    }
-    __syncthreads();
-    for (int idx = threadIdx.x; idx < G * D; idx += kThreads) {
-        const int g = idx / D, d = idx % D;
-        float M = sm_m[0][g];
-#pragma unroll
-        for (int w = 1; w < kWarps; ++w) M = fmaxf(M, sm_m[w][g]);
-        float o = 0.f, l = 0.f;
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) {
-            const float sc = fast_exp2(sm_m[w][g] - M);
-            o = fmaf(sc, sm_acc[w][g][d], o);
-            l = fmaf(sc, sm_l[w][g], l);
-        }
-        const size_t slot = ((size_t)n * Hq + h * G + g) * n_slots + split;
-        part_o[slot * D + d] = o;
-        if (d == 0) part_ml[slot] = make_float2(M, l);
-    }
-}
-
-// One CTA of D/4 threads per (query head, session): merge the session's used slots.
 // Where combine puts a finished row.  n_peers == 0: o [N][Hq][D] of this call.  n_peers > 0
 // (head-tensor-parallel decode): row (n, hq) of every output peers[k] [N][hq_total][D] at head
 // head0 + hq -- the all-gather of the heads' outputs, done by the kernel that finishes them
@@ -181,76 +37,75 @@ struct CombineOut {
     int n_peers, head0, hq_total;
 };
 
+// One warp per (session, query head) row, four rows per CTA.  The row's used slots (its own
+// splits, then the shared-prefix chunks) are merged by log-sum-exp: lanes read the slots'
+// (max, sum) pairs in parallel and reduce them with shuffles, then each lane accumulates 4
+// output dims over the slots (independent 16-byte loads, weights broadcast by shuffle).
+constexpr int kCombineRows = 4;
+
 template <int D>
-__global__ void __launch_bounds__(D / 4)
+__global__ void __launch_bounds__(32 * kCombineRows)
 combine_kernel(const float* __restrict__ part_o, const float2* __restrict__ part_ml,
                const int32_t* __restrict__ seq_lens, const CombineOut out,
                float* __restrict__ lse, int Hq, int max_pages, int pages_per_split,
                int first_page, int n_slots, int prefix_slot0, int n_prefix_chunks) {
-    const int hq = blockIdx.x, n = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int hq = blockIdx.x * kCombineRows + warp, n = blockIdx.y;
+    if (hq >= Hq) return;
     const int L = min(max(seq_lens[n], 0), max_pages * kPage);
     const int npages = (L + kPage - 1) / kPage;
     const int rem = npages - first_page;
     const int nsplit = rem > 0 ? (rem + pages_per_split - 1) / pages_per_split : 0;
+    const int total = nsplit + (L > 0 ? n_prefix_chunks : 0);
     const size_t row = (size_t)n * Hq + hq;
     const float2* ml = part_ml + row * n_slots;
     const float* po = part_o + row * n_slots * D;
+    auto slot = [&](int j) { return j < nsplit ? j : prefix_slot0 + (j - nsplit); };
 
-    const int npre = L > 0 ? n_prefix_chunks : 0;
     float M = -INFINITY;
-    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, ml[s].x);
-    for (int s = 0; s < npre; ++s) M = fmaxf(M, ml[prefix_slot0 + s].x);
+    for (int j = lane; j < total; j += 32) M = fmaxf(M, ml[slot(j)].x);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
 
-    const int d0 = threadIdx.x * 4;
+    constexpr int kLanes = D / 4;                          // lanes that own 4 output dims
+    const int d0 = 4 * lane;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     float l = 0.f;
-    auto add_slot = [&](int s) {
-        const float2 e = ml[s];
-        const float w = fast_exp2(e.x - M);
-        const float4 v = *reinterpret_cast<const float4*>(po + (size_t)s * D + d0);
-        acc.x = fmaf(w, v.x, acc.x); acc.y = fmaf(w, v.y, acc.y);
-        acc.z = fmaf(w, v.z, acc.z); acc.w = fmaf(w, v.w, acc.w);
-        l = fmaf(w, e.y, l);
-    };
-    for (int s = 0; s < nsplit; ++s) add_slot(s);
-    for (int s = 0; s < npre; ++s) add_slot(prefix_slot0 + s);
-
-    const float inv = l > 0.f ? 1.f / l : 0.f;
-    uint2 packed;
-    packed.x = pack_bf16x2(acc.x * inv, acc.y * inv);
-    packed.y = pack_bf16x2(acc.z * inv, acc.w * inv);
-    if (out.n_peers == 0) {
-        *reinterpret_cast<uint2*>(out.o + row * D + d0) = packed;
-    } else {
-        const size_t grow = ((size_t)n * out.hq_total + out.head0 + hq) * D + d0;
-        for (int k = 0; k < out.n_peers; ++k) *reinterpret_cast<uint2*>(out.peers[k] + grow) = packed;
-        __threadfence_system();                      // visible to the peers before the kernel ends
+    for (int j0 = 0; j0 < total; j0 += 32) {
+        float w = 0.f;
+        if (j0 + lane < total) {
+            const float2 e = ml[slot(j0 + lane)];
+            w = fast_exp2(e.x - M);
+            l = fmaf(w, e.y, l);
+        }
+        const int cnt = min(32, total - j0);
+#pragma unroll 4
+        for (int t = 0; t < cnt; ++t) {
+            const float wt = __shfl_sync(0xffffffffu, w, t);
+            if (lane < kLanes) {
+                const float4 v = *reinterpret_cast<const float4*>(po + (size_t)slot(j0 + t) * D + d0);
+                acc.x = fmaf(wt, v.x, acc.x); acc.y = fmaf(wt, v.y, acc.y);
+                acc.z = fmaf(wt, v.z, acc.z); acc.w = fmaf(wt, v.w, acc.w);
+            }
+        }
     }
-    if (lse != nullptr && threadIdx.x == 0) lse[row] = l > 0.f ? (M + log2f(l)) * kLn2 : -INFINITY;
-}
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
 
-template <int D, int G>
-void launch_split(dim3 grid, cudaStream_t st, const uint16_t* q, const uint16_t* kp,
-                  const uint16_t* vp, const int32_t* bt, const int32_t* lens, float* po,
-                  float2* pml, int Hq, int Hkv, int num_pages, int max_pages, int pps,
-                  int first_page, int n_slots, float qscale) {
-    split_kernel<D, G><<<grid, kThreads, 0, st>>>(q, kp, vp, bt, lens, po, pml, Hq, Hkv, num_pages,
-                                                  max_pages, pps, first_page, n_slots, qscale);
-}
-
-template <int D>
-int dispatch_group(int G, dim3 grid, cudaStream_t st, const uint16_t* q, const uint16_t* kp,
-                   const uint16_t* vp, const int32_t* bt, const int32_t* lens, float* po,
-                   float2* pml, int Hq, int Hkv, int num_pages, int max_pages, int pps,
-                   int first_page, int n_slots, float qscale) {
-    switch (G) {
-        case 1: launch_split<D, 1>(grid, st, q, kp, vp, bt, lens, po, pml, Hq, Hkv, num_pages, max_pages, pps, first_page, n_slots, qscale); break;
-        case 2: launch_split<D, 2>(grid, st, q, kp, vp, bt, lens, po, pml, Hq, Hkv, num_pages, max_pages, pps, first_page, n_slots, qscale); break;
-        case 4: launch_split<D, 4>(grid, st, q, kp, vp, bt, lens, po, pml, Hq, Hkv, num_pages, max_pages, pps, first_page, n_slots, qscale); break;
-        case 8: launch_split<D, 8>(grid, st, q, kp, vp, bt, lens, po, pml, Hq, Hkv, num_pages, max_pages, pps, first_page, n_slots, qscale); break;
-        default: return set_error(LF_EINVAL, "decode: Hq/Hkv must be 1, 2, 4 or 8 (got %d)", G);
+    if (lane < kLanes) {
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        uint2 packed;
+        packed.x = pack_bf16x2(acc.x * inv, acc.y * inv);
+        packed.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+        if (out.n_peers == 0) {
+            *reinterpret_cast<uint2*>(out.o + row * D + d0) = packed;
+        } else {
+            const size_t grow = ((size_t)n * out.hq_total + out.head0 + hq) * D + d0;
+            for (int k = 0; k < out.n_peers; ++k) *reinterpret_cast<uint2*>(out.peers[k] + grow) = packed;
+            __threadfence_system();                  // visible to the peers before the kernel ends
+        }
     }
-    return LF_OK;
+    if (lse != nullptr && lane == 0) lse[row] = l > 0.f ? (M + log2f(l)) * kLn2 : -INFINITY;
 }
 
 // Slots [0, suffix_splits) hold the per-session splits after the prefix; slots
@@ -258,10 +113,11 @@ int dispatch_group(int G, dim3 grid, cudaStream_t st, const uint16_t* q, const u
 inline int suffix_splits(int max_pages, int pps, int n_prefix) {
     return (max_pages - n_prefix + pps - 1) / pps;
 }
-// Shared-prefix pages are cut into chunks of at most 32 pages (one tensor-core CTA each) so the
-// prefix pass fills the GPU even when sessions use long splits.
-// Shared-prefix chunk: 16..32 pages (a small split size must not shred the prefix into many
-// partials for the combine step).
+// Shared-prefix pages are cut into chunks of 16..32 pages (one tensor-core work item each): the
+// prefix pass then has work for many SMs even when sessions use long splits, and a small split
+// size does not shred the prefix into many partials for the combine step.  (Chunks of 16 pages
+// for few sessions measured slower: the extra partials cost the combine more than the shorter
+// items save.)
 inline int prefix_chunk_pages(int pps) { return pps < 16 ? 16 : (pps < 32 ? pps : 32); }
 inline int prefix_chunks(int pps, int n_prefix) {
     const int c = prefix_chunk_pages(pps);
@@ -341,6 +197,14 @@ extern "C" int lf_decode_default_split(int num_seqs, int num_kv_heads, int max_p
     clear_error();
     return LF_OK;
 }
+
+// Defined in decode_mma.cu: the per-session split pass on the warp-level tensor-core MMA.
+namespace lf { namespace decode {
+int launch_split_mma(dim3 grid, cudaStream_t st, const uint16_t* q, const uint16_t* kp,
+                     const uint16_t* vp, const int32_t* bt, const int32_t* lens, float* po,
+                     float2* pml, int Hq, int Hkv, int D, int num_pages, int max_pages, int pps,
+                     int first_page, int n_slots, float qscale);
+}}
 
 // Defined in decode_prefix.cu: shared-prefix partials, one pass over the prefix pages per
 // group of sessions.
@@ -453,15 +317,10 @@ static int decode_impl(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* 
     if (max_split > 0) {
         dim3 grid(max_split, num_kv_heads, num_seqs);
         LF_CHECK_ARG(max_split <= 2147483647, "decode: too many splits");
-        int rc = head_dim == 128
-                     ? decode::dispatch_group<128>(G, grid, st, q16, k_pages, v_pages, block_table,
-                                                   seq_lens, po, pml, num_q_heads, num_kv_heads,
-                                                   num_pages, max_pages, pages_per_split, num_prefix_pages,
-                                                   n_slots, qscale)
-                     : decode::dispatch_group<64>(G, grid, st, q16, k_pages, v_pages, block_table,
-                                                  seq_lens, po, pml, num_q_heads, num_kv_heads,
-                                                  num_pages, max_pages, pages_per_split, num_prefix_pages,
-                                                  n_slots, qscale);
+        int rc = decode::launch_split_mma(grid, st, q16, k_pages, v_pages, block_table, seq_lens,
+                                          po, pml, num_q_heads, num_kv_heads, head_dim, num_pages,
+                                          max_pages, pages_per_split, num_prefix_pages, n_slots,
+                                          qscale);
         if (rc == LF_OK) rc = launch_status("decode split");
         if (rc != LF_OK) {
             if (overlap) {                                    // keep the fork closed
@@ -481,15 +340,16 @@ static int decode_impl(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* 
     }
     if (prof) LF_CHECK_CUDA(cudaEventRecord(g_prof_end, st));
     if (overlap) LF_CHECK_CUDA(cudaStreamWaitEvent(st, side->join, 0));   // prefix partials ready
-    dim3 cgrid(num_q_heads, num_seqs);
+    dim3 cgrid((num_q_heads + decode::kCombineRows - 1) / decode::kCombineRows, num_seqs);
+    constexpr int cthreads = 32 * decode::kCombineRows;
     if (head_dim == 128)
-        decode::combine_kernel<128><<<cgrid, 32, 0, st>>>(po, pml, seq_lens, out, lse, num_q_heads,
-                                                          max_pages, pages_per_split, num_prefix_pages,
-                                                          n_slots, max_split, n_prefix_chunks);
+        decode::combine_kernel<128><<<cgrid, cthreads, 0, st>>>(po, pml, seq_lens, out, lse, num_q_heads,
+                                                                max_pages, pages_per_split, num_prefix_pages,
+                                                                n_slots, max_split, n_prefix_chunks);
     else
-        decode::combine_kernel<64><<<cgrid, 16, 0, st>>>(po, pml, seq_lens, out, lse, num_q_heads,
-                                                         max_pages, pages_per_split, num_prefix_pages,
-                                                         n_slots, max_split, n_prefix_chunks);
+        decode::combine_kernel<64><<<cgrid, cthreads, 0, st>>>(po, pml, seq_lens, out, lse, num_q_heads,
+                                                               max_pages, pages_per_split, num_prefix_pages,
+                                                               n_slots, max_split, n_prefix_chunks);
     return launch_status("decode combine");
 }
 
@@ -657,7 +517,6 @@ extern "C" int lf_decode_fwd_noalloc(const lf_bf16* q, const lf_bf16* k_pages,
     if (rc != LF_OK) return rc;
 
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const int G = num_q_heads / num_kv_heads;
     const int n_slots = decode::num_slots(max_pages, pps, num_prefix_pages);
     const int max_split = decode::suffix_splits(max_pages, pps, num_prefix_pages);
     const int n_prefix_chunks = decode::prefix_chunks(pps, num_prefix_pages);
@@ -674,28 +533,22 @@ extern "C" int lf_decode_fwd_noalloc(const lf_bf16* q, const lf_bf16* k_pages,
     }
     if (max_split > 0) {
         dim3 grid(max_split, num_kv_heads, num_seqs);
-        rc = head_dim == 128
-                 ? decode::dispatch_group<128>(G, grid, st, q, k_pages, v_pages, block_table,
-                                               seq_lens, po, pml, num_q_heads, num_kv_heads,
-                                               num_pages, max_pages, pps, num_prefix_pages,
-                                               n_slots, qscale)
-                 : decode::dispatch_group<64>(G, grid, st, q, k_pages, v_pages, block_table,
-                                              seq_lens, po, pml, num_q_heads, num_kv_heads,
-                                              num_pages, max_pages, pps, num_prefix_pages,
-                                              n_slots, qscale);
+        rc = decode::launch_split_mma(grid, st, q, k_pages, v_pages, block_table, seq_lens, po,
+                                      pml, num_q_heads, num_kv_heads, head_dim, num_pages,
+                                      max_pages, pps, num_prefix_pages, n_slots, qscale);
         if (rc != LF_OK) return rc;
         rc = launch_status("decode noalloc split");
         if (rc != LF_OK) return rc;
     }
-    dim3 cgrid(num_q_heads, num_seqs);
+    dim3 cgrid((num_q_heads + decode::kCombineRows - 1) / decode::kCombineRows, num_seqs);
     if (head_dim == 128)
-        decode::combine_kernel<128><<<cgrid, 32, 0, st>>>(po, pml, seq_lens,
+        decode::combine_kernel<128><<<cgrid, 32 * decode::kCombineRows, 0, st>>>(po, pml, seq_lens,
                                                           decode::CombineOut{o, nullptr, 0, 0, num_q_heads},
                                                           lse, num_q_heads,
                                                           max_pages, pps, num_prefix_pages,
                                                           n_slots, max_split, n_prefix_chunks);
     else
-        decode::combine_kernel<64><<<cgrid, 16, 0, st>>>(po, pml, seq_lens,
+        decode::combine_kernel<64><<<cgrid, 32 * decode::kCombineRows, 0, st>>>(po, pml, seq_lens,
                                                          decode::CombineOut{o, nullptr, 0, 0, num_q_heads},
                                                          lse, num_q_heads,
                                                          max_pages, pps, num_prefix_pages,

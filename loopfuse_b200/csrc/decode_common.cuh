@@ -1,5 +1,6 @@
-// Lane layout and reductions shared by the paged decode kernels (decode.cu,
-// decode_prefix.cu).  A page row of D bf16 is read by D/8 lanes, 16 bytes each.
+// Paged-decode constants shared by decode.cu, decode_mma.cu and decode_prefix.cu, and the lane
+// layout and reductions of the CUDA-core shared-prefix kernel (decode_prefix.cu, head_dim 64):
+// a page row of D bf16 is read by D/8 lanes, 16 bytes each.
 #pragma once
 
 #include "lf_common.cuh"

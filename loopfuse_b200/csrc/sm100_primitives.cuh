@@ -117,6 +117,12 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+// Orders this thread's earlier generic-proxy accesses of shared memory before later
+// async-proxy (bulk copy) accesses.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // ---- packed fp32 pairs (sm_100a f32x2 arithmetic) -------------------------------------------
 __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
     uint64_t r;

@@ -47,6 +47,41 @@ class LlamaConfig:
                 "num_kv_heads": self.kv_heads, "head_dim": self.head_dim, "dtype": "bf16"}
 
 
+class OpTimer:
+    """CUDA-event attribution of one forward's GPU time to op classes.
+
+    ``lap(name)`` records an event on the current stream and charges the time since the previous
+    event to ``name``.  Call ``start()`` first; ``totals()`` (after a sync) returns milliseconds
+    per name.  To keep host launch gaps out of the measured spans, ``start`` can hold the stream
+    in a device-side spin (``hold_cycles``) while the host enqueues the whole forward."""
+
+    def __init__(self):
+        self.events: List[tuple] = []
+
+    def start(self, hold_cycles: int = 0) -> None:
+        if hold_cycles:
+            torch.cuda._sleep(int(hold_cycles))
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        self.events = [(None, ev)]
+
+    def lap(self, name: str) -> None:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        self.events.append((name, ev))
+
+    def totals(self) -> dict:
+        out: dict = {}
+        for (_, a), (name, b) in zip(self.events, self.events[1:]):
+            out[name] = out.get(name, 0.0) + a.elapsed_time(b)
+        return out
+
+
+def _lap(timer: Optional[OpTimer], name: str) -> None:
+    if timer is not None:
+        timer.lap(name)
+
+
 class LlamaShaped:
     def __init__(self, cfg: LlamaConfig, device="cuda", seed: int = 0, std: float = 0.02):
         self.cfg = cfg
@@ -125,21 +160,31 @@ class LlamaShaped:
             x.add_(delta)
         return self._rmsnorm(x, w) if w is not None else None
 
-    def _mlp_block(self, x: torch.Tensor, attn: torch.Tensor, l: int):
+    def _mlp_block(self, x: torch.Tensor, attn: torch.Tensor, l: int,
+                   timer: Optional[OpTimer] = None):
         """Rest of layer ``l`` after attention: output projection, residual, FFN norm, SwiGLU
         FFN, residual, and the next layer's input norm.  Returns (x, normed input of l + 1)."""
         c = self.cfg
-        h = self._norm_in(x, attn @ self.wo[l], self.ffn_norm[l])
+        o = attn @ self.wo[l]
+        _lap(timer, "o_gemm")
+        h = self._norm_in(x, o, self.ffn_norm[l])
+        _lap(timer, "add_rmsnorm")
         gu = h @ self.w13[l]
+        _lap(timer, "gate_up_gemm")
         act = mo.swiglu(gu) if self.fused_ops else F.silu(gu[:, :c.ffn]) * gu[:, c.ffn:]
+        _lap(timer, "swiglu")
         nxt = self.attn_norm[l + 1] if l + 1 < c.layers else None
-        return x, self._norm_in(x, act @ self.w2[l], nxt)
+        d = act @ self.w2[l]
+        _lap(timer, "down_gemm")
+        out = self._norm_in(x, d, nxt)
+        _lap(timer, "add_rmsnorm")
+        return x, out
 
     # -- forward ------------------------------------------------------------------------------
     @torch.no_grad()
     def forward(self, tokens: torch.Tensor, pool: KVPool, states: Sequence[KVState],
                 counts: Sequence[int], n_prefix_pages: int = 0,
-                return_logits: bool = False) -> torch.Tensor:
+                return_logits: bool = False, timer: Optional[OpTimer] = None) -> torch.Tensor:
         c = self.cfg
         counts = [int(x) for x in counts]
         T = sum(counts)
@@ -164,14 +209,19 @@ class LlamaShaped:
                                               pps, n_prefix_pages)
             if self._ws is None or self._ws.numel() < need:
                 self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        if timer is not None:
+            timer.lap("setup")
         x = self.embed[tokens]
         nq, nk = c.q_heads * c.head_dim, c.kv_heads * c.head_dim
         h = self._norm_in(x, None, self.attn_norm[0])
+        _lap(timer, "embed_norm")
         for l in range(c.layers):
             qkv = h @ self.wqkv[l]
+            _lap(timer, "qkv_gemm")
             if self.fused_qkv:
                 q = torch.empty((T, c.q_heads, c.head_dim), dtype=qkv.dtype, device=self.device)
                 pool.write_qkv(states, start, l, qkv, q, counts, rope=rope, index=index)
+                _lap(timer, "qkv_rope_append")
             else:
                 q = self._rope(qkv[:, :nq].view(T, c.q_heads, c.head_dim), cos, sin).contiguous()
                 k = self._rope(qkv[:, nq:nq + nk].view(T, c.kv_heads, c.head_dim), cos, sin)
@@ -184,11 +234,15 @@ class LlamaShaped:
                                      workspace=self._ws)
             else:
                 a = att.prefill_paged(q, kp, vp, table, cu, lens, max(counts))
-            x, h = self._mlp_block(x, a.view(T, nq), l)
+            _lap(timer, "attention")
+            x, h = self._mlp_block(x, a.view(T, nq), l, timer)
         last = torch.tensor(counts, device=self.device).cumsum(0) - 1
         h = self._norm_in(x[last].contiguous(), None, self.final_norm)
         logits = h @ self.lm_head
-        return logits.float() if return_logits else torch.argmax(logits, dim=-1)
+        _lap(timer, "lm_head")
+        out = logits.float() if return_logits else torch.argmax(logits, dim=-1)
+        _lap(timer, "argmax")
+        return out
 
     # -- AgentExecutor model contract ------------------------------------------------------------
     def prefill(self, tokens: torch.Tensor, kv_state: KVState, attention=None) -> torch.Tensor:
