@@ -67,6 +67,9 @@ def parse_args():
     ap.add_argument("--workload", choices=["decode", "agent"], default="decode")
     ap.add_argument("--agent-sessions", type=int, default=512)
     ap.add_argument("--agent-steps", type=int, default=10)
+    ap.add_argument("--agent-world", type=int, default=0,
+                    help="with --workload agent on one GPU: run rank 0's share of a job over this "
+                         "many GPUs (one rank's work, not a scaling measurement)")
     ap.add_argument("--cpu-sample", type=int, default=8, help="sessions in the CPU sample")
     ap.add_argument("--sustain-ms", type=float, default=1200.0,
                     help="length of the sustained decode window sampled for clocks")
@@ -285,7 +288,8 @@ def agent_measure(args, grp) -> dict:
     rng = np.random.default_rng(cfg.seed)
     work = np.minimum(rng.geometric(1.0 / cfg.tool_len_mean, size=(cfg.sessions, cfg.steps)),
                       cfg.tool_len_cap).sum(axis=1)
-    mine = lpt_assign([float(x) for x in work], grp.world)[grp.rank]
+    shards = args.agent_world if (args.agent_world and grp.world == 1) else grp.world
+    mine = lpt_assign([float(x) for x in work], shards)[grp.rank]
     model = LlamaShaped(LlamaConfig(), device=grp.device, seed=args.seed)
     loop = AgentLoop(model, cfg, session_ids=mine, device=grp.device)
     # warm-up: a short loop on two sessions touches every code path
@@ -300,6 +304,19 @@ def agent_measure(args, grp) -> dict:
     st = loop.run(profile_ops=True)
     wall = grp.max(st.wall_s)
     steps = grp.sum(float(st.steps_done))
+    if shards != grp.world:                  # one rank's share, run alone
+        tool = max(float(loop.tool_lat[i, :cfg.steps - 1].sum()) for i in mine)
+        return {"metric": "agent steps/s of one rank's share", "value": round(steps / wall, 2),
+                "unit": "steps/s", "n_gpus": 1, "steps": int(steps), "wall_s": round(wall, 3),
+                "share_of": shards, "sessions_on_rank0": len(mine),
+                "longest_tool_chain_s": round(tool, 3),
+                "rank0": {"wall_s": round(st.wall_s, 3), "decode_iters": st.decode_iters,
+                          "prefill_batches": st.prefill_batches, "prefill_s": round(st.prefill_s, 3),
+                          "decode_s": round(st.decode_s, 3), "spec_s": round(st.spec_s, 3),
+                          "kernels": st.kernels},
+                "workload": AGENT_WORKLOAD, "sessions": cfg.sessions,
+                "steps_per_session": cfg.steps, "ms_per_step": round(1000 * wall / max(1.0, steps), 3),
+                "parallelism": f"rank 0 of {shards} (LPT on tool-output length), alone on one GPU"}
     res = {"metric": "agent steps/s", "value": round(steps / wall, 2), "unit": "steps/s",
            "n_gpus": grp.world, "steps": int(steps), "wall_s": round(wall, 3),
            "ms_per_step": round(1000 * wall / max(1.0, steps / grp.world), 3),
@@ -339,6 +356,8 @@ def run_agent(args):
                            "sessions_on_rank0": r["sessions_on_rank0"],
                            "parallelism": r["parallelism"]},
                 "rank0": r["rank0"],
+                **({"share_of": r["share_of"], "longest_tool_chain_s": r["longest_tool_chain_s"]}
+                   if "share_of" in r else {}),
                 "e2e": {"value": r["value"], "unit": "steps/s",
                         "h2d_bytes_per_step": None, "d2h_bytes_per_step": None}}
         print(json.dumps(line), flush=True)
@@ -775,11 +794,11 @@ def main():
             "per_rank": [{"rank": r, "ms_per_step": round(a, 4), "split_kernel_ms": round(b, 4),
                           "unique_bytes": int(c), "split_bytes": int(d)}
                          for r, (a, b, c, d) in enumerate(per_rank)],
-            "roofline": {"bound": "hbm", "kernel": "decode split (per-session pages)",
+            "roofline": {"bound": "hbm", "kernel": "decode split (per-session pages, mma::split_mma_kernel)",
                          "achieved": round(achieved, 1) if achieved else None,
                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / peaks["hbm_gbs"], 4) if achieved else None,
-                         "traffic": profile_traffic("decode_split_256sess.txt"),
+                         "traffic": profile_traffic("decode_split_mma_16sess.txt"),
                          "kernel_ms": round(split_ms, 4), "kernel_bytes": split_bytes,
                          "op_frac": round(value / world / peaks["hbm_gbs"], 4),
                          "peak_source": peaks["source"]},
