@@ -115,9 +115,9 @@ inline int suffix_splits(int max_pages, int pps, int n_prefix) {
 }
 // Shared-prefix pages are cut into chunks of 16..32 pages (one tensor-core work item each): the
 // prefix pass then has work for many SMs even when sessions use long splits, and a small split
-// size does not shred the prefix into many partials for the combine step.  (Chunks of 16 pages
-// for few sessions measured slower: the extra partials cost the combine more than the shorter
-// items save.)
+// size does not shred the prefix into many partials for the combine step.  (Chunks of 16 or 8
+// pages for 64 sessions measured slower, with either launch order: the extra items hold more SMs
+// and the extra partials cost the combine more than the shorter items save.)
 inline int prefix_chunk_pages(int pps) { return pps < 16 ? 16 : (pps < 32 ? pps : 32); }
 inline int prefix_chunks(int pps, int n_prefix) {
     const int c = prefix_chunk_pages(pps);
