@@ -100,6 +100,7 @@ class AgentLoopStats:
     spec_s: float = 0.0
     idle_waits: int = 0
     kernels: Optional[dict] = None     # per-kernel-class attribution (run(profile_ops=True))
+    final_lengths: List[int] = field(default_factory=list)   # tokens per session at the end
 
 
 class AgentLoop:
@@ -329,6 +330,7 @@ class AgentLoop:
         torch.cuda.synchronize(self.device)
         stats.wall_s = time.perf_counter() - t_start
         stats.steps_per_s = stats.steps_done / stats.wall_s
+        stats.final_lengths = [s.state.current_len for s in sessions]
         if profile_ops:                       # after the timed loop, on its final state
             stats.kernels = self._profile_ops(sessions)
         pool.release_all(states)

@@ -117,3 +117,33 @@ def test_graphed_decode_matches_eager_decode():
     assert sum(a == b for a, b in zip(flat_e, flat_g)) >= 0.9 * len(flat_e)
     for a, b in zip(k_e, k_g):                                # the sessions' own K, every layer
         assert (a.float() - b.float()).abs().max().item() < 0.05
+
+
+def test_agent_loop_speculation_changes_no_session_length_and_returns_every_page():
+    """Speculative prefill of the observation template in idle windows moves work earlier but
+    not its amount: with speculation on and off every session ends with the same number of
+    tokens (prompt, questions, templates, tool outputs, decoded tokens), and after the loop
+    every page except the system prompt's is back in the free queue."""
+    m = LlamaShaped(SMALL, seed=6)
+    runs = {}
+    for spec in (True, False):
+        cfg = AgentLoopConfig(sessions=8, steps=3, prefix_tokens=64, question_tokens=16,
+                              decode_tokens=4, tool_ms=20.0, tool_len_mean=12, tool_len_cap=30,
+                              spec_tokens=4, speculative=spec, seed=7)
+        loop = AgentLoop(m, cfg)
+        st = loop.run()
+        assert st.steps_done == cfg.sessions * cfg.steps
+        runs[spec] = (st, loop)
+        snap = loop.pool.snapshot()
+        root_pages = cfg.prefix_tokens // 16
+        pad_pages = 1 if cfg.graphs else 0                 # the graphs' padding session
+        assert len(snap["free_queue"]) == loop.pool.num_pages - root_pages - pad_pages
+    st_on, loop_on = runs[True]
+    st_off, _ = runs[False]
+    assert st_on.spec_batches > 0 and st_off.spec_batches == 0
+    assert st_on.final_lengths == st_off.final_lengths
+    c = loop_on.cfg
+    want = [c.prefix_tokens + c.question_tokens + c.steps * (c.decode_tokens - 1) +
+            sum(c.spec_tokens + int(loop_on.tool_len[i, k]) for k in range(c.steps - 1))
+            for i in range(c.sessions)]
+    assert st_on.final_lengths == want
