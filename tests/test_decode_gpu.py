@@ -40,8 +40,11 @@ def test_decode_shapes(hq, hkv, d):
     assert (lse.cpu() - ref_lse).abs().max().item() < 1e-3
 
 
-@pytest.mark.parametrize("pps", [1, 2, 3, 8, 64])
+@pytest.mark.parametrize("pps", [1, 2, 3, 8, 64, 200, 256])
 def test_decode_split_sizes(pps):
+    """Split sizes from one page (hundreds of partials per session for the combine) to a whole
+    256-page session in one split (a warp then takes 64 pages: its page ids come in two batches
+    of 32)."""
     lengths = [5, 160, 161, 999, 4096]
     w = decode_inputs(N=5, lengths=lengths, prefix_tokens=0, seed=4)
     o = att.paged_decode(w.q, w.k_pages, w.v_pages, w.block_table, w.seq_lens, pages_per_split=pps)
