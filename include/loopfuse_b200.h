@@ -296,6 +296,19 @@ int lf_add_rmsnorm(lf_bf16* x, const lf_bf16* delta, const lf_bf16* w, lf_bf16* 
  * counterpart (the reference models are GPT-style). */
 int lf_swiglu(const lf_bf16* gu, lf_bf16* out, int rows, int ffn, void* stream);
 
+/* Decode-batch projection y[M, N] = x[M, K] . w[K, N] (bf16 in and out, fp32 accumulation),
+ * for 1 <= M <= 128: the weight-streaming tcgen05 GEMM the decoder's decode steps use for their
+ * dense projections (the projection half of kernels/triton/fused_ln_qkv.py:64-72, which computes
+ * a row's QKV output one weight column at a time; here for any projection, the whole batch
+ * sharing each weight tile).  Persistent: min(sm_count,
+ * units) CTAs split the 128-column x 64-row weight units evenly; column blocks shared by two or
+ * more CTAs are summed from fp32 partials in a fixed order, so results are deterministic.
+ * x [M][K], w [K][N], y [M][N] contiguous; N and K multiples of 8; buffers 16-byte aligned.
+ * workspace: lf_gemm_skinny_workspace_size bytes (same M, N, K, sm_count). */
+int lf_gemm_skinny_workspace_size(int M, int N, int K, int sm_count, size_t* bytes);
+int lf_gemm_skinny(const lf_bf16* x, const lf_bf16* w, lf_bf16* y, int M, int N, int K,
+                   void* workspace, size_t workspace_bytes, int sm_count, void* stream);
+
 /* ---- prefix-hash dedup (KV fusion by content) ------------------------------------------
  * The reference's KV fusion is a compile-time pass keyed on IR positions
  * (passes/kv_fusion.py:80-107) and its pool has no sharing (runtime/kv_pool.py:28-235), so

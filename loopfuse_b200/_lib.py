@@ -71,6 +71,8 @@ _SIGS = {
                           _P, _P, _P, c_int, c_int, c_int, _P],
     "lf_add_rmsnorm": [_P, _P, _P, _P, c_int, c_int, c_float, _P],
     "lf_swiglu": [_P, _P, c_int, c_int, _P],
+    "lf_gemm_skinny_workspace_size": [c_int, c_int, c_int, c_int, POINTER(c_size_t)],
+    "lf_gemm_skinny": [_P, _P, _P, c_int, c_int, c_int, _P, c_size_t, c_int, _P],
     "lf_decode_fwd_gather": [_P, _P, _P, _P, _P, c_int, _P, c_int, c_int, c_int, _P, _P, c_size_t,
                              c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_float, _P],
     "lf_ipc_export": [_P, _P, POINTER(c_size_t)],

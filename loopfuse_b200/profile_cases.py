@@ -7,6 +7,7 @@
     python -m loopfuse_b200.profile_cases epilogue [--tokens 16384] [--reps 3]
     python -m loopfuse_b200.profile_cases dedup [--sessions 512] [--reps 3]
     python -m loopfuse_b200.profile_cases fusion_decode [--sessions 64] [--private 600] [--reps 3]
+    python -m loopfuse_b200.profile_cases projections [--rows 64] [--reps 3] [--only qkv]
 
 Each case builds its inputs, runs one warm-up launch and then ``--reps`` launches of the op,
 so a capture can skip the warm-up (``-s``) and take one to three launches (``-c``).  The decode
@@ -187,10 +188,73 @@ def run_dedup(sessions: int, reps: int) -> None:
     print(f"dedup sessions={sessions} pages={4096 // 16}")
 
 
+LLAMA_PROJECTIONS = {"qkv": (4096, 6144), "o": (4096, 4096), "gate_up": (4096, 28672),
+                     "down": (14336, 4096), "lm_head": (4096, 128256)}
+
+
+def run_projections(rows: int, reps: int, only: str = "") -> None:
+    """The decoder's dense projections (Llama-3-8B shapes) at a decode batch of ``rows`` rows:
+    ``lf_gemm_skinny`` against the library GEMM (``torch.matmul``), both replayed from CUDA
+    graphs over enough weight copies (>= 4, >= 512 MB) that no launch finds its weights in L2.
+    Prints the CUDA-event time per call, the weight bytes per call and the max difference of the
+    two results.  Under a profiler the graphs still replay, one kernel launch per call."""
+    from . import model_ops as mo
+    names = [only] if only else list(LLAMA_PROJECTIONS)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    for name in names:
+        k, n = LLAMA_PROJECTIONS[name]
+        copies = max(4, -(-(512 << 20) // (k * n * 2)))
+        ws = [(torch.randn(k, n, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+              for _ in range(copies)]
+        x = torch.randn(rows, k, generator=g, device="cuda").to(torch.bfloat16)
+        y0 = torch.empty(rows, n, dtype=torch.bfloat16, device="cuda")
+        y1 = torch.empty_like(y0)
+        wsp = torch.empty(mo.skinny_workspace_bytes(rows, n, k, torch.cuda.get_device_properties(0)
+                                                    .multi_processor_count),
+                          dtype=torch.uint8, device="cuda")
+        calls = {"skinny": lambda w: mo.gemm_skinny(x, w, out=y0, workspace=wsp),
+                 "library": lambda w: torch.matmul(x, w, out=y1)}
+        res = {}
+        for tag, fn in calls.items():
+            for w in ws:
+                fn(w)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                with torch.cuda.graph(graph):
+                    for w in ws:
+                        fn(w)
+            torch.cuda.current_stream().wait_stream(side)
+            graph.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(max(1, reps)):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            res[tag] = e0.elapsed_time(e1) * 1e3 / (max(1, reps) * copies)
+        fn = calls["skinny"]
+        fn(ws[-1])
+        torch.matmul(x, ws[-1], out=y1)
+        torch.cuda.synchronize()
+        diff = (y0.float() - y1.float()).abs().max().item()
+        wb = k * n * 2
+        print(f"projection {name} M={rows} K={k} N={n} weight_bytes={wb} "
+              f"skinny_us={res['skinny']:.2f} ({wb / res['skinny'] / 1e3:.0f} GB/s) "
+              f"library_us={res['library']:.2f} ({wb / res['library'] / 1e3:.0f} GB/s) "
+              f"max_diff={diff:.3e}", flush=True)
+        del ws
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["decode", "prefill", "pool", "paged", "epilogue", "dedup",
-                                     "fusion_decode"])
+                                     "fusion_decode", "projections"])
+    ap.add_argument("--only", default="")
+    ap.add_argument("--rows", type=int, default=64)
     ap.add_argument("--private", type=int, default=600)
     ap.add_argument("--sessions", type=int, default=32)
     ap.add_argument("--batch", type=int, default=2)
@@ -204,6 +268,8 @@ def main(argv=None) -> None:
         run_decode(a.sessions, a.reps, a.pages_per_split)
     elif a.case == "fusion_decode":
         run_fusion_decode(a.sessions, a.reps, a.pages_per_split, a.private)
+    elif a.case == "projections":
+        run_projections(a.rows, a.reps, a.only)
     elif a.case == "prefill":
         run_prefill(a.batch, a.seq, a.reps)
     elif a.case == "paged":

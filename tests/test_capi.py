@@ -63,3 +63,22 @@ def test_default_split_size_is_a_power_of_two_between_32_and_128_pages():
         pps = default_pages_per_split(n, hkv, max_pages, npre)
         assert pps in (32, 64, 128), (n, hkv, max_pages, npre, pps)
     assert default_pages_per_split(256, 8, 2048, 128) == 128      # the 256-session decode
+
+
+def test_skinny_gemm_workspace_and_argument_checks():
+    """Partial-sum workspace = min(SMs, units) CTAs x 2 slots x M x 128 fp32; bad shapes are
+    rejected on the host before any launch."""
+    lib = _lib.lib()
+    n = ctypes.c_size_t(0)
+    _lib.call("lf_gemm_skinny_workspace_size", 64, 6144, 4096, 148, ctypes.byref(n))
+    assert n.value == 148 * 2 * 64 * 128 * 4
+    _lib.call("lf_gemm_skinny_workspace_size", 3, 136, 72, 148, ctypes.byref(n))
+    assert n.value == 4 * 2 * 3 * 128 * 4          # 2 column blocks x 2 K chunks = 4 units
+    p = 1 << 20                                     # aligned stand-in address, never touched
+    assert lib.lf_gemm_skinny(p, p, p, 129, 64, 64, p, 1 << 30, 148, None) == _lib.LF_EINVAL
+    assert b"M <= 128" in lib.lf_last_error()
+    assert lib.lf_gemm_skinny(p, p, p, 8, 60, 64, p, 1 << 30, 148, None) == _lib.LF_EINVAL
+    assert lib.lf_gemm_skinny(p + 2, p, p, 8, 64, 64, p, 1 << 30, 148, None) == _lib.LF_EINVAL
+    assert lib.lf_gemm_skinny(p, p, p, 8, 64, 64, p, 16, 148, None) == _lib.LF_EINVAL
+    assert b"workspace" in lib.lf_last_error()
+    assert lib.lf_gemm_skinny(None, p, p, 8, 64, 64, p, 1 << 30, 148, None) == _lib.LF_EINVAL
