@@ -77,8 +77,11 @@ constexpr uint32_t kPageBoxBytes = 16 * 64 * 2;   // 2 KB: [16 rows][64 dims]
 constexpr uint32_t OFF_Q = 0;                            // 2 tiles
 constexpr uint32_t OFF_K = OFF_Q + 2 * kTileBytes;       // 2 stages
 constexpr uint32_t OFF_V = OFF_K + 2 * kTileBytes;       // 2 stages
-constexpr uint32_t OFF_BAR = OFF_V + 2 * kTileBytes;
+constexpr uint32_t OFF_EPI = OFF_V + 2 * kTileBytes;     // epilogue staging, 4 KB per softmax warp
+constexpr uint32_t kEpiWarpBytes = 4096;
+constexpr uint32_t OFF_BAR = OFF_EPI + 8 * kEpiWarpBytes;
 constexpr uint32_t kSmemBytes = OFF_BAR + 256 + 1024;
+static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
 constexpr uint32_t kColS = 0, kColO = 256, kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;
 
@@ -117,8 +120,8 @@ struct Item {
     int nbk;
 };
 
-// Coordinates of work item w.  Called by all 32 lanes of a warp (prefix mode reduces over the
-// item's sessions with shuffles).
+// Coordinates of work item w.  Every role computes them (no shared state), with all 32 lanes
+// of a warp (prefix mode may reduce over the tile's sessions with shuffles).
 template <Mode M>
 __device__ __forceinline__ Item item_coords(const Params& p, int w, int lane) {
     Item it;
@@ -168,6 +171,10 @@ __device__ __forceinline__ Item item_coords(const Params& p, int w, int lane) {
             it.nb[t] = n;
         }
     } else {
+        // The item's pages come from one session's block-table row (src).  Fast path: the tile's
+        // first session n0 covers the whole chunk (one length read).  Otherwise the longest
+        // session of the tile is taken (a lane-parallel scan) and the chunk is cut at its
+        // length; rows shorter than the chunk are masked per row by the softmax (key_limit).
         const int qtile = w % p.n_qtiles;
         const int rest = w / p.n_qtiles;
         it.h = rest % p.Hkv;
@@ -176,22 +183,27 @@ __device__ __forceinline__ Item item_coords(const Params& p, int w, int lane) {
         it.n0 = qtile * spt;
         it.p_begin = it.chunk * p.chunk_pages;
         it.p_end = min(it.p_begin + p.chunk_pages, p.n_prefix);
-        int best_len = -1, best = it.n0;
-        for (int k = lane; k < spt; k += 32) {
-            const int n = it.n0 + k;
-            if (n < p.N) {
-                const int L = min(max(p.lens[n], 0), p.max_pages * 16);
-                if (L > best_len) { best_len = L; best = n; }
+        const int L0 = min(max(p.lens[it.n0], 0), p.max_pages * 16);
+        if ((L0 + 15) / 16 >= it.p_end) {
+            it.src = it.n0;
+        } else {
+            int best_len = -1, best = it.n0;
+            for (int k = lane; k < spt; k += 32) {
+                const int n = it.n0 + k;
+                if (n < p.N) {
+                    const int L = min(max(p.lens[n], 0), p.max_pages * 16);
+                    if (L > best_len) { best_len = L; best = n; }
+                }
             }
-        }
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
-            const int ol = __shfl_xor_sync(0xffffffffu, best_len, off);
-            const int on = __shfl_xor_sync(0xffffffffu, best, off);
-            if (ol > best_len || (ol == best_len && on < best)) { best_len = ol; best = on; }
+            for (int off = 16; off > 0; off >>= 1) {
+                const int ol = __shfl_xor_sync(0xffffffffu, best_len, off);
+                const int on = __shfl_xor_sync(0xffffffffu, best, off);
+                if (ol > best_len || (ol == best_len && on < best)) { best_len = ol; best = on; }
+            }
+            it.src = best;
+            it.p_end = min(it.p_end, (max(best_len, 0) + 15) / 16);
         }
-        it.src = best;
-        it.p_end = min(it.p_end, (max(best_len, 0) + 15) / 16);
         const int n = it.p_end > it.p_begin ? (it.p_end - it.p_begin + 7) / 8 : 0;
         it.nb[0] = it.nb[1] = n;
     }
@@ -260,9 +272,73 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
         int g = 0, qi = 0;
         bool ok = true;
         for (int w = blockIdx.x; w < p.n_items && ok; w += gridDim.x) {
+            // Paged modes: a 128-key tile is 8 pages x (HD / 64) boxes of [16 rows][64 dims].
+            // Lane 2 * page + half issues one box of K and one of V, so the whole tile's boxes go
+            // out at once; its page id is fetched one block ahead.  Prefix mode reads the first
+            // block's ids from the tile's first session before the item's coordinates are known
+            // (the usual source row), so the two reads overlap.
+            const int pg = lane >> 1, hf = lane & 1;
+            const bool loader = lane < 16 && hf < HD / 64;
+            int spec_src = -1, spec_page = -1;
+            if constexpr (M == Mode::Prefix) {
+                const int rest = w / p.n_qtiles;
+                spec_src = (w % p.n_qtiles) * (2 * BM / p.G);
+                const int pb = (rest / p.Hkv) * p.chunk_pages;
+                const int pi = pb + pg;
+                if (loader && pi < min(pb + p.chunk_pages, p.n_prefix))
+                    spec_page = __ldg(p.bt + (size_t)spec_src * p.max_pages + pi);
+            }
+            // Prefix mode: Q's coordinates need no loads, so its load goes out first; an item that
+            // turns out empty (every session of the tile ends before the chunk) leaves this Q
+            // phase to the MMA warp, which takes it without MMAs.
+            bool q_early = false;
+            if constexpr (M == Mode::Prefix) {
+                if (lane == 0) {
+                    if (qi > 0) ok = mbar_wait(bar(Q_EMPTY), (qi - 1) & 1, abort_flag, 12);
+                    if (ok) {
+                        mbar_arrive_expect_tx(bar(Q_FULL), 2 * kLoadBytes);
+                        const int h = (w / p.n_qtiles) % p.Hkv;
+#pragma unroll
+                        for (int t = 0; t < 2; ++t)
+#pragma unroll
+                            for (int hf = 0; hf < HD / 64; ++hf)
+                                tma_load_4d(sbase + OFF_Q + t * kTileBytes + hf * kHalfBytes, &tmq,
+                                            bar(Q_FULL), hf * 64, 0, h, spec_src + t * (BM / p.G));
+                    }
+                }
+                if (!(ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0)) break;
+                q_early = true;
+            }
             const Item it = item_coords<M>(p, w, lane);
-            if (it.nbk == 0) continue;
-            if (lane == 0) {
+            if (it.nbk == 0) {
+                if (q_early) ++qi;
+                continue;
+            }
+            const int32_t* bt_row = (M == Mode::Dense) ? nullptr
+                                    : (M == Mode::Prefix) ? p.bt + (size_t)it.src * p.max_pages
+                                                          : p.bt + (size_t)it.sess * p.max_pages;
+            const int kv_head = (M == Mode::Paged) ? it.kvh : it.h;
+            auto to_row = [&](int page) -> int {
+                if (static_cast<unsigned>(page) >= static_cast<unsigned>(p.num_pages)) {
+                    atomicCAS(&g_device_error, 0, 201);
+                    return p.num_pages * p.Hkv;                  // out of range: zeros
+                }
+                return page * p.Hkv + kv_head;
+            };
+            auto page_row = [&](int j) -> int {
+                const int pi = it.p_begin + j * 8 + pg;
+                return (loader && pi < it.p_end) ? to_row(__ldg(bt_row + pi)) : p.num_pages * p.Hkv;
+            };
+            int row = 0;
+            if constexpr (M == Mode::Prefix) {
+                if (it.src == spec_src) {
+                    const int pi = it.p_begin + pg;
+                    row = (loader && pi < it.p_end) ? to_row(spec_page) : p.num_pages * p.Hkv;
+                } else {
+                    row = page_row(0);
+                }
+            }
+            if (lane == 0 && !q_early) {
                 if (qi > 0) ok = mbar_wait(bar(Q_EMPTY), (qi - 1) & 1, abort_flag, 12);
                 if (ok) {
                     mbar_arrive_expect_tx(bar(Q_FULL), 2 * kLoadBytes);
@@ -305,29 +381,9 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                     }
                 }
             } else if (ok) {
-                // Pages: a 128-key tile is 8 pages x (HD / 64) boxes of [16 rows][64 dims].
-                // Lane 2 * page + half issues one box of K and one of V, so the whole tile's
-                // boxes go out at once; its page id is fetched one block ahead.  Lane 0 waits
-                // for the free stage and posts the tile's byte count before the boxes are
-                // issued (the shuffle orders it).
-                const int32_t* bt_row = (M == Mode::Prefix) ? p.bt + (size_t)it.src * p.max_pages
-                                                            : p.bt + (size_t)it.sess * p.max_pages;
-                const int kv_head = (M == Mode::Paged) ? it.kvh : it.h;
-                const int pg = lane >> 1, hf = lane & 1;
-                const bool loader = lane < 16 && hf < HD / 64;
-                auto page_row = [&](int j) -> int {
-                    const int pi = it.p_begin + j * 8 + pg;
-                    int row = p.num_pages * p.Hkv;                   // out of range: zeros
-                    if (loader && pi < it.p_end) {
-                        const int page = __ldg(bt_row + pi);
-                        if (static_cast<unsigned>(page) >= static_cast<unsigned>(p.num_pages))
-                            atomicCAS(&g_device_error, 0, 201);
-                        else
-                            row = page * p.Hkv + kv_head;
-                    }
-                    return row;
-                };
-                int row = page_row(0);
+                // Lane 0 waits for the free stage and posts the tile's byte count before the
+                // boxes are issued (the shuffle orders it).
+                if constexpr (M == Mode::Paged) row = page_row(0);
                 const uint32_t box = hf * kHalfBytes + pg * kPageBoxBytes;
                 for (int j = 0; j < it.nbk; ++j) {
                     const int gj = g + j, st = gj & 1;
@@ -401,7 +457,17 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
         bool ok = true;
         for (int w = blockIdx.x; w < p.n_items && ok; w += gridDim.x) {
             const Item it = item_coords<M>(p, w, lane);
-            if (it.nbk == 0) continue;
+            if (it.nbk == 0) {
+                if constexpr (M == Mode::Prefix) {
+                    // the producer loaded this item's Q before it knew the item was empty
+                    const uint32_t b1[1] = {bar(Q_FULL)};
+                    const uint32_t p1[1] = {static_cast<uint32_t>(qi & 1)};
+                    if (!(ok = vote(mbar_wait_all(b1, p1, abort_flag, 3)))) break;
+                    if (lane == 0) mbar_arrive(bar(Q_EMPTY));
+                    ++qi;
+                }
+                continue;
+            }
             {
                 const uint32_t bs[2] = {bar(Q_FULL), bar(K_FULL + (g & 1))};
                 const uint32_t ps[2] = {static_cast<uint32_t>(qi & 1), static_cast<uint32_t>((g >> 1) & 1)};
@@ -646,9 +712,23 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                         p.lse[orow] = l_run > 0.f ? (m_run + log2f(l_run)) * kLn2 : -INFINITY;
                 }
             } else {
+                // prefix partials: slot (n, hq, slot0 + chunk) of part_o [N][Hq][n_slots][D] fp32
+                // holds O / l as bf16 in its first D * 2 bytes (the epilogue is bound by the SM's
+                // store bandwidth: half the bytes of fp32), (m, l) go to part_ml.  TMEM gives each
+                // thread one row and consecutive rows live in different slots, so the rows go out
+                // through this warp's staging tile in shared memory: each lane writes its row's
+                // 16-byte pieces at XOR-swizzled positions (no bank conflicts), then groups of 4
+                // lanes store one row's 64 contiguous bytes (8 rows per store).
+                auto slot_of = [&](int rr) -> size_t {
+                    const int nn = it.n0 + rr / p.G;
+                    return ((size_t)nn * (p.Hkv * p.G) + it.h * p.G + rr % p.G) * p.n_slots +
+                           p.slot0 + it.chunk;
+                };
                 const int rr = t * BM + row;
-                const size_t slot =
-                    ((size_t)n * (p.Hkv * p.G) + it.h * p.G + rr % p.G) * p.n_slots + p.slot0 + it.chunk;
+                const int n_row = it.n0 + rr / p.G;
+                const int g0 = ((warp - 4) & 3) * 32;     // tile row of this warp's lane 0
+                const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+                uint4* stage = reinterpret_cast<uint4*>(smem + OFF_EPI + (warp - 4) * kEpiWarpBytes);
 #pragma unroll 1
                 for (int cc = 0; cc < HD / 32; ++cc) {
                     uint32_t r[32];
@@ -659,15 +739,28 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
 #pragma unroll
                         for (int i = 0; i < 32; ++i) r[i] = 0u;
                     }
-                    if (n < p.N) {
-                        float4* dst = reinterpret_cast<float4*>(p.part_o + slot * HD + cc * 32);
+                    __syncwarp();                      // the previous chunk's reads are done
 #pragma unroll
-                        for (int v = 0; v < 8; ++v)
-                            dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
-                                                 __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+                    for (int v = 0; v < 4; ++v) {
+                        uint4 wv;
+                        wv.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]) * inv, __uint_as_float(r[8 * v + 1]) * inv);
+                        wv.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * inv, __uint_as_float(r[8 * v + 3]) * inv);
+                        wv.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * inv, __uint_as_float(r[8 * v + 5]) * inv);
+                        wv.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * inv, __uint_as_float(r[8 * v + 7]) * inv);
+                        stage[lane * 4 + (v ^ ((lane >> 1) & 3))] = wv;
+                    }
+                    __syncwarp();
+                    // 64 bytes of a row per 4 lanes, 8 rows per store
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int rl = i * 8 + (lane >> 2), q = lane & 3;
+                        const uint4 v = stage[rl * 4 + (q ^ ((rl >> 1) & 3))];
+                        const int rr2 = t * BM + g0 + rl;
+                        if (it.n0 + rr2 / p.G < p.N)
+                            reinterpret_cast<uint4*>(p.part_o + slot_of(rr2) * HD)[cc * 4 + q] = v;
                     }
                 }
-                if (n < p.N) p.part_ml[slot] = make_float2(m_run, l_run);
+                if (n_row < p.N) p.part_ml[slot_of(rr)] = make_float2(m_run, l_run);
             }
         }
     }

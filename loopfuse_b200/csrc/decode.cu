@@ -38,17 +38,22 @@ struct CombineOut {
 };
 
 // One warp per (session, query head) row, four rows per CTA.  The row's used slots (its own
-// splits, then the shared-prefix chunks) are merged by log-sum-exp: lanes read the slots'
-// (max, sum) pairs in parallel and reduce them with shuffles, then each lane accumulates 4
-// output dims over the slots (independent 16-byte loads, weights broadcast by shuffle).
+// splits, then the shared-prefix chunks) are merged by log-sum-exp.  A split slot holds its
+// unnormalised output in fp32; a prefix slot holds O / l in bf16 (first D * 2 bytes of the
+// slot), scaled back by its l here.  Only the session length is read before the slots'
+// addresses are known; then every lane loads its slot's (max, sum) pair and the first kPrefetch
+// slots' output vectors (4 dims per lane) at once, so a row costs two dependent memory round
+// trips, not one per batch of slots.  Rows with more slots take the rest in a loop.
 constexpr int kCombineRows = 4;
+constexpr int kPrefetch = 12;
 
 template <int D>
 __global__ void __launch_bounds__(32 * kCombineRows)
 combine_kernel(const float* __restrict__ part_o, const float2* __restrict__ part_ml,
                const int32_t* __restrict__ seq_lens, const CombineOut out,
                float* __restrict__ lse, int Hq, int max_pages, int pages_per_split,
-               int first_page, int n_slots, int prefix_slot0, int n_prefix_chunks) {
+               int first_page, int n_slots, int prefix_slot0, int n_prefix_chunks,
+               int prefix_chunk_pages) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int hq = blockIdx.x * kCombineRows + warp, n = blockIdx.y;
     if (hq >= Hq) return;
@@ -56,36 +61,69 @@ combine_kernel(const float* __restrict__ part_o, const float2* __restrict__ part
     const int npages = (L + kPage - 1) / kPage;
     const int rem = npages - first_page;
     const int nsplit = rem > 0 ? (rem + pages_per_split - 1) / pages_per_split : 0;
-    const int total = nsplit + (L > 0 ? n_prefix_chunks : 0);
+    // shared-prefix chunks that hold some of this session's keys (a session shorter than the
+    // prefix uses only the first ones; the prefix pass may skip the rest for its whole tile)
+    const int pre_pages = min(first_page, npages);
+    const int nchunk = n_prefix_chunks > 0
+                           ? min(n_prefix_chunks, (pre_pages + prefix_chunk_pages - 1) / prefix_chunk_pages)
+                           : 0;
+    const int total = nsplit + nchunk;
     const size_t row = (size_t)n * Hq + hq;
     const float2* ml = part_ml + row * n_slots;
     const float* po = part_o + row * n_slots * D;
     auto slot = [&](int j) { return j < nsplit ? j : prefix_slot0 + (j - nsplit); };
 
-    float M = -INFINITY;
-    for (int j = lane; j < total; j += 32) M = fmaxf(M, ml[slot(j)].x);
+    constexpr int kLanes = D / 4;                          // lanes that own 4 output dims
+    const int d0 = 4 * lane;
+    const bool owner = lane < kLanes;
+    auto load = [&](int j) -> float4 {                     // slot j's 4 dims of this lane
+        const float* base = po + (size_t)slot(j) * D;
+        if (j < nsplit) return *reinterpret_cast<const float4*>(base + d0);
+        const uint2 b = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(base) + d0);
+        return make_float4(bf16lo_to_f32(b.x), bf16hi_to_f32(b.x), bf16lo_to_f32(b.y), bf16hi_to_f32(b.y));
+    };
+    float2 e = make_float2(-INFINITY, 0.f);
+    if (lane < total) e = ml[slot(lane)];
+    float4 v[kPrefetch];
+#pragma unroll
+    for (int t = 0; t < kPrefetch; ++t)
+        v[t] = (t < total && owner) ? load(t) : make_float4(0.f, 0.f, 0.f, 0.f);
+
+    float M = e.x;
+    for (int j = lane + 32; j < total; j += 32) M = fmaxf(M, ml[slot(j)].x);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
 
-    constexpr int kLanes = D / 4;                          // lanes that own 4 output dims
-    const int d0 = 4 * lane;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     float l = 0.f;
+    float w = lane < total ? fast_exp2(e.x - M) : 0.f;
+    if (lane < total) l = w * e.y;
+    // weight of slot j's vector: w for a split slot, w * l for a (normalised) prefix slot
+    float wv = lane >= nsplit ? w * e.y : w;
+#pragma unroll
+    for (int t = 0; t < kPrefetch; ++t) {
+        const float wt = __shfl_sync(0xffffffffu, wv, t);
+        acc.x = fmaf(wt, v[t].x, acc.x); acc.y = fmaf(wt, v[t].y, acc.y);
+        acc.z = fmaf(wt, v[t].z, acc.z); acc.w = fmaf(wt, v[t].w, acc.w);
+    }
     for (int j0 = 0; j0 < total; j0 += 32) {
-        float w = 0.f;
-        if (j0 + lane < total) {
-            const float2 e = ml[slot(j0 + lane)];
-            w = fast_exp2(e.x - M);
-            l = fmaf(w, e.y, l);
+        if (j0 > 0) {
+            wv = 0.f;
+            if (j0 + lane < total) {
+                const float2 ej = ml[slot(j0 + lane)];
+                const float wj = fast_exp2(ej.x - M);
+                l = fmaf(wj, ej.y, l);
+                wv = j0 + lane >= nsplit ? wj * ej.y : wj;
+            }
         }
-        const int cnt = min(32, total - j0);
+        const int t_end = min(32, total - j0);
 #pragma unroll 4
-        for (int t = 0; t < cnt; ++t) {
-            const float wt = __shfl_sync(0xffffffffu, w, t);
-            if (lane < kLanes) {
-                const float4 v = *reinterpret_cast<const float4*>(po + (size_t)slot(j0 + t) * D + d0);
-                acc.x = fmaf(wt, v.x, acc.x); acc.y = fmaf(wt, v.y, acc.y);
-                acc.z = fmaf(wt, v.z, acc.z); acc.w = fmaf(wt, v.w, acc.w);
+        for (int t = (j0 == 0 ? kPrefetch : 0); t < t_end; ++t) {
+            const float wt = __shfl_sync(0xffffffffu, wv, t);
+            if (owner) {
+                const float4 vt = load(j0 + t);
+                acc.x = fmaf(wt, vt.x, acc.x); acc.y = fmaf(wt, vt.y, acc.y);
+                acc.z = fmaf(wt, vt.z, acc.z); acc.w = fmaf(wt, vt.w, acc.w);
             }
         }
     }
@@ -346,11 +384,13 @@ static int decode_impl(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* 
     if (head_dim == 128)
         decode::combine_kernel<128><<<cgrid, cthreads, 0, st>>>(po, pml, seq_lens, out, lse, num_q_heads,
                                                                 max_pages, pages_per_split, num_prefix_pages,
-                                                                n_slots, max_split, n_prefix_chunks);
+                                                                n_slots, max_split, n_prefix_chunks,
+                                                                decode::prefix_chunk_pages(pages_per_split));
     else
         decode::combine_kernel<64><<<cgrid, cthreads, 0, st>>>(po, pml, seq_lens, out, lse, num_q_heads,
                                                                max_pages, pages_per_split, num_prefix_pages,
-                                                               n_slots, max_split, n_prefix_chunks);
+                                                               n_slots, max_split, n_prefix_chunks,
+                                                               decode::prefix_chunk_pages(pages_per_split));
     return launch_status("decode combine");
 }
 
@@ -547,12 +587,14 @@ extern "C" int lf_decode_fwd_noalloc(const lf_bf16* q, const lf_bf16* k_pages,
                                                           decode::CombineOut{o, nullptr, 0, 0, num_q_heads},
                                                           lse, num_q_heads,
                                                           max_pages, pps, num_prefix_pages,
-                                                          n_slots, max_split, n_prefix_chunks);
+                                                          n_slots, max_split, n_prefix_chunks,
+                                                          decode::prefix_chunk_pages(pps));
     else
         decode::combine_kernel<64><<<cgrid, 32 * decode::kCombineRows, 0, st>>>(po, pml, seq_lens,
                                                          decode::CombineOut{o, nullptr, 0, 0, num_q_heads},
                                                          lse, num_q_heads,
                                                          max_pages, pps, num_prefix_pages,
-                                                         n_slots, max_split, n_prefix_chunks);
+                                                         n_slots, max_split, n_prefix_chunks,
+                                                         decode::prefix_chunk_pages(pps));
     return launch_status("decode noalloc combine");
 }

@@ -183,6 +183,8 @@ prefix_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kp,
         __syncthreads();
     }
 
+    // Prefix slots hold the normalised output O / l as bf16 in the first D * 2 bytes of the
+    // slot (half the bytes of fp32; the combine scales it back by l), plus (m, l) in part_ml.
 #pragma unroll
     for (int i = 0; i < SPW; ++i) {
         if (sess[i] >= N) continue;
@@ -193,13 +195,22 @@ prefix_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kp,
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
                     acc[i][g][j] += __shfl_xor_sync(0xffffffffu, acc[i][g][j], off);
+        float inv_l[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float lg = __shfl_sync(0xffffffffu, l_run[i], chunk_of_head<D, G>(g));
+            inv_l[g] = lg > 0.f ? 1.f / lg : 0.f;
+        }
         if (sub == 0) {
 #pragma unroll
             for (int g = 0; g < G; ++g) {
                 const size_t slot = ((size_t)sess[i] * Hq + h * G + g) * n_slots + slot0 + chunk;
-                float4* dst = reinterpret_cast<float4*>(part_o + slot * D + 8 * c);
-                dst[0] = make_float4(acc[i][g][0], acc[i][g][1], acc[i][g][2], acc[i][g][3]);
-                dst[1] = make_float4(acc[i][g][4], acc[i][g][5], acc[i][g][6], acc[i][g][7]);
+                uint4 pk;
+                pk.x = pack_bf16x2(acc[i][g][0] * inv_l[g], acc[i][g][1] * inv_l[g]);
+                pk.y = pack_bf16x2(acc[i][g][2] * inv_l[g], acc[i][g][3] * inv_l[g]);
+                pk.z = pack_bf16x2(acc[i][g][4] * inv_l[g], acc[i][g][5] * inv_l[g]);
+                pk.w = pack_bf16x2(acc[i][g][6] * inv_l[g], acc[i][g][7] * inv_l[g]);
+                reinterpret_cast<uint4*>(part_o + slot * D)[c] = pk;
             }
             if (c == chunk_of_head<D, G>(hl)) {
                 const size_t slot = ((size_t)sess[i] * Hq + h * G + hl) * n_slots + slot0 + chunk;

@@ -112,3 +112,21 @@ def test_decode_sessions_entirely_inside_the_shared_prefix():
     o = att.paged_decode(w.q, w.k_pages, w.v_pages, w.block_table, w.seq_lens,
                          num_prefix_pages=w.n_prefix_pages)
     _check(o, _oracle(w)[0], "prefix only")
+
+
+@pytest.mark.parametrize("lengths", [[100] * 64 + [3000], [40, 100] * 32 + [2100, 5000],
+                                     [20, 3000, 5000, 257]])
+def test_decode_sessions_shorter_than_the_prefix(lengths):
+    """Sessions shorter than the shared prefix hold only the prefix pages they cover (the rest
+    of their row is -1).  The prefix pass works on tiles of 64 sessions (4 query heads each): a
+    tile whose sessions all end before a prefix chunk skips that chunk, and the combine must not
+    read its slot -- the workspace is filled with NaN bytes first.  The last case's first
+    session covers no chunk, so every item takes its pages from the tile's longest session."""
+    w = decode_inputs(N=len(lengths), lengths=lengths, prefix_tokens=2048, seed=9)
+    max_pages = w.block_table.shape[1]
+    need = att.decode_workspace_bytes(len(lengths), w.q.shape[1], w.q.shape[2], max_pages, 8,
+                                      w.n_prefix_pages)
+    ws = torch.full((need,), 255, dtype=torch.uint8, device="cuda")
+    o = att.paged_decode(w.q, w.k_pages, w.v_pages, w.block_table, w.seq_lens,
+                         num_prefix_pages=w.n_prefix_pages, pages_per_split=8, workspace=ws)
+    _check(o, _oracle(w)[0], f"lengths={lengths}")
