@@ -151,19 +151,27 @@ combine_kernel(const float* __restrict__ part_o, const float2* __restrict__ part
 inline int suffix_splits(int max_pages, int pps, int n_prefix) {
     return (max_pages - n_prefix + pps - 1) / pps;
 }
-// Shared-prefix pages are cut into chunks of 16..32 pages (one tensor-core work item each): the
-// prefix pass then has work for many SMs even when sessions use long splits, and a small split
-// size does not shred the prefix into many partials for the combine step.  (Chunks of 16 or 8
-// pages for 64 sessions measured slower, with either launch order: the extra items hold more SMs
-// and the extra partials cost the combine more than the shorter items save.)
-inline int prefix_chunk_pages(int pps) { return pps < 16 ? 16 : (pps < 32 ? pps : 32); }
-inline int prefix_chunks(int pps, int n_prefix) {
-    const int c = prefix_chunk_pages(pps);
-    return (n_prefix + c - 1) / c;
+// Shared-prefix pages are cut into chunks; a tensor-core work item is one (pair of 128-row query
+// tiles, KV head, chunk).  Longer chunks amortise an item's fixed cost (start-up loads, epilogue)
+// and leave fewer partials for the combine; shorter ones make more items, which matters when the
+// prefix pass is the critical path (few sessions, short private runs).  The chunk starts at 32
+// pages and doubles while the pass keeps at least 64 items.  Measured on B200 with a 4096-token
+// prefix and 600-1600 private tokens per session: 64 sessions -> 32 pages, 96-128 -> 64,
+// 256 -> 128, 512 -> 256, each the fastest of 16..256 pages or within 3% of it.
+constexpr int kMinPrefixChunk = 32;
+inline int prefix_chunk_pages(int N, int G, int Hkv, int n_prefix) {
+    const long tiles = ((long)N * G + 255) / 256;
+    int c = kMinPrefixChunk;
+    while (c < n_prefix && tiles * Hkv * ((n_prefix + 2L * c - 1) / (2L * c)) >= 64) c *= 2;
+    return c;
 }
-inline int num_slots(int max_pages, int pages_per_split, int num_prefix_pages) {
+inline int prefix_chunks(int chunk_pages, int n_prefix) {
+    return (n_prefix + chunk_pages - 1) / chunk_pages;
+}
+// chunk_pages = kMinPrefixChunk gives the most slots any launch can use (workspace sizing).
+inline int num_slots(int max_pages, int pages_per_split, int num_prefix_pages, int chunk_pages) {
     return suffix_splits(max_pages, pages_per_split, num_prefix_pages) +
-           prefix_chunks(pages_per_split, num_prefix_pages);
+           prefix_chunks(chunk_pages, num_prefix_pages);
 }
 
 }  // namespace decode
@@ -178,7 +186,8 @@ extern "C" int lf_decode_workspace_size(int num_seqs, int num_q_heads, int head_
     LF_CHECK_ARG(num_seqs >= 0 && num_q_heads > 0 && head_dim > 0 && max_pages > 0 &&
                      pages_per_split > 0 && num_prefix_pages >= 0,
                  "decode: bad workspace arguments");
-    const size_t slots = (size_t)decode::num_slots(max_pages, pages_per_split, num_prefix_pages);
+    const size_t slots = (size_t)decode::num_slots(max_pages, pages_per_split, num_prefix_pages,
+                                                   decode::kMinPrefixChunk);
     *bytes = (size_t)num_seqs * num_q_heads * slots * ((size_t)head_dim * sizeof(float) + sizeof(float2));
     clear_error();
     return LF_OK;
@@ -317,9 +326,10 @@ static int decode_impl(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* 
 
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int G = num_q_heads / num_kv_heads;
-    const int n_slots = decode::num_slots(max_pages, pages_per_split, num_prefix_pages);
+    const int chunk = decode::prefix_chunk_pages(num_seqs, G, num_kv_heads, num_prefix_pages);
+    const int n_slots = decode::num_slots(max_pages, pages_per_split, num_prefix_pages, chunk);
     const int max_split = decode::suffix_splits(max_pages, pages_per_split, num_prefix_pages);
-    const int n_prefix_chunks = decode::prefix_chunks(pages_per_split, num_prefix_pages);
+    const int n_prefix_chunks = decode::prefix_chunks(chunk, num_prefix_pages);
     float* po = static_cast<float*>(workspace);
     float2* pml = reinterpret_cast<float2*>(po + (size_t)num_seqs * num_q_heads * n_slots * head_dim);
     const float qscale = scale * kLog2e;
@@ -344,7 +354,7 @@ static int decode_impl(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* 
         return decode::launch_prefix(q16, k_pages, v_pages, block_table, seq_lens, po, pml,
                                      num_seqs, num_q_heads, num_kv_heads, head_dim, num_pages,
                                      max_pages, num_prefix_pages,
-                                     decode::prefix_chunk_pages(pages_per_split), n_slots,
+                                     chunk, n_slots,
                                      max_split, qscale, pst);
     };
     if (num_prefix_pages > 0 && !overlap) {
@@ -384,13 +394,11 @@ static int decode_impl(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* 
     if (head_dim == 128)
         decode::combine_kernel<128><<<cgrid, cthreads, 0, st>>>(po, pml, seq_lens, out, lse, num_q_heads,
                                                                 max_pages, pages_per_split, num_prefix_pages,
-                                                                n_slots, max_split, n_prefix_chunks,
-                                                                decode::prefix_chunk_pages(pages_per_split));
+                                                                n_slots, max_split, n_prefix_chunks, chunk);
     else
         decode::combine_kernel<64><<<cgrid, cthreads, 0, st>>>(po, pml, seq_lens, out, lse, num_q_heads,
                                                                max_pages, pages_per_split, num_prefix_pages,
-                                                               n_slots, max_split, n_prefix_chunks,
-                                                               decode::prefix_chunk_pages(pages_per_split));
+                                                               n_slots, max_split, n_prefix_chunks, chunk);
     return launch_status("decode combine");
 }
 
@@ -509,8 +517,9 @@ static int noalloc_scratch(void** out) {
     return LF_OK;
 }
 
-static size_t partial_bytes(int N, int Hq, int D, int max_pages, int pps, int n_prefix) {
-    return (size_t)N * Hq * (size_t)num_slots(max_pages, pps, n_prefix) *
+static size_t partial_bytes(int N, int Hq, int D, int max_pages, int pps, int n_prefix,
+                            int chunk) {
+    return (size_t)N * Hq * (size_t)num_slots(max_pages, pps, n_prefix, chunk) *
            ((size_t)D * sizeof(float) + sizeof(float2));
 }
 
@@ -541,12 +550,15 @@ extern "C" int lf_decode_fwd_noalloc(const lf_bf16* q, const lf_bf16* k_pages,
     int rc = decode::device_sm_count(&sms);
     if (rc != LF_OK) return rc;
     int pps = decode::default_split(num_seqs, num_kv_heads, max_pages, num_prefix_pages, sms);
-    while (decode::partial_bytes(num_seqs, num_q_heads, head_dim, max_pages, pps, num_prefix_pages) >
+    const int chunk = decode::prefix_chunk_pages(num_seqs, num_q_heads / num_kv_heads, num_kv_heads,
+                                                 num_prefix_pages);
+    while (decode::partial_bytes(num_seqs, num_q_heads, head_dim, max_pages, pps, num_prefix_pages,
+                                 chunk) >
                (size_t)LF_DECODE_NOALLOC_SCRATCH_BYTES &&
            pps < max_pages)
         pps = pps * 2 < max_pages ? pps * 2 : max_pages;
     const size_t need =
-        decode::partial_bytes(num_seqs, num_q_heads, head_dim, max_pages, pps, num_prefix_pages);
+        decode::partial_bytes(num_seqs, num_q_heads, head_dim, max_pages, pps, num_prefix_pages, chunk);
     LF_CHECK_ARG(need <= (size_t)LF_DECODE_NOALLOC_SCRATCH_BYTES,
                  "decode noalloc: %d sessions x %d heads need %zu bytes of partials even with one "
                  "split per session; the fixed scratch holds %u bytes (use lf_decode_fwd with a "
@@ -558,9 +570,9 @@ extern "C" int lf_decode_fwd_noalloc(const lf_bf16* q, const lf_bf16* k_pages,
     if (rc != LF_OK) return rc;
 
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const int n_slots = decode::num_slots(max_pages, pps, num_prefix_pages);
+    const int n_slots = decode::num_slots(max_pages, pps, num_prefix_pages, chunk);
     const int max_split = decode::suffix_splits(max_pages, pps, num_prefix_pages);
-    const int n_prefix_chunks = decode::prefix_chunks(pps, num_prefix_pages);
+    const int n_prefix_chunks = decode::prefix_chunks(chunk, num_prefix_pages);
     float* po = static_cast<float*>(scratch);
     float2* pml = reinterpret_cast<float2*>(po + (size_t)num_seqs * num_q_heads * n_slots * head_dim);
     const float qscale = scale * kLog2e;
@@ -568,7 +580,7 @@ extern "C" int lf_decode_fwd_noalloc(const lf_bf16* q, const lf_bf16* k_pages,
     if (num_prefix_pages > 0) {
         rc = decode::launch_prefix(q, k_pages, v_pages, block_table, seq_lens, po, pml, num_seqs,
                                    num_q_heads, num_kv_heads, head_dim, num_pages, max_pages,
-                                   num_prefix_pages, decode::prefix_chunk_pages(pps), n_slots, max_split,
+                                   num_prefix_pages, chunk, n_slots, max_split,
                                    qscale, st);
         if (rc != LF_OK) return rc;
     }
@@ -587,14 +599,12 @@ extern "C" int lf_decode_fwd_noalloc(const lf_bf16* q, const lf_bf16* k_pages,
                                                           decode::CombineOut{o, nullptr, 0, 0, num_q_heads},
                                                           lse, num_q_heads,
                                                           max_pages, pps, num_prefix_pages,
-                                                          n_slots, max_split, n_prefix_chunks,
-                                                          decode::prefix_chunk_pages(pps));
+                                                          n_slots, max_split, n_prefix_chunks, chunk);
     else
         decode::combine_kernel<64><<<cgrid, 32 * decode::kCombineRows, 0, st>>>(po, pml, seq_lens,
                                                          decode::CombineOut{o, nullptr, 0, 0, num_q_heads},
                                                          lse, num_q_heads,
                                                          max_pages, pps, num_prefix_pages,
-                                                         n_slots, max_split, n_prefix_chunks,
-                                                         decode::prefix_chunk_pages(pps));
+                                                         n_slots, max_split, n_prefix_chunks, chunk);
     return launch_status("decode noalloc combine");
 }

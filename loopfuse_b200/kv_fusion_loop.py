@@ -15,8 +15,8 @@ by the paged split-KV decode with the shared prefix, in every one of ``layers`` 
 Attention shapes are Llama-3-8B's (32 layers, 32 query / 8 KV heads, head_dim 128, bf16);
 the K/V/q values are synthetic (no model weights are involved).
 
-After the first decode iteration, every decode iteration (all sessions, one token, every layer)
-is replayed from one CUDA graph: the session set is fixed, so its shapes are.
+Every decode iteration (all sessions, one token, every layer) is replayed from one CUDA graph,
+captured during setup: the session set is fixed, so its shapes are.
 
 Per step it reports the algorithmic HBM bytes the attention reads with prefix sharing
 (``bytes_read``: every page a kernel must touch, the prefix once per decode call) and without
@@ -52,7 +52,7 @@ class FusionLoopConfig:
     tool_mean: float = 120.0
     tool_cap: int = 1024
     seed: int = 0
-    graphs: bool = True          # decode iterations after the first replayed from a CUDA graph
+    graphs: bool = True          # decode iterations replayed from a CUDA graph captured in setup
 
 
 def tool_lengths(cfg: FusionLoopConfig) -> np.ndarray:
@@ -144,6 +144,22 @@ class FusionLoop:
             ids = [self.spec.open_seq() for _ in range(c.sessions)]
             self.spec.fork(self.root.slot_id, ids, c.prefix_tokens)
             self._check()
+        S = self.sessions
+        self._dec_idx = pool.batch_index(S, [1] * len(S))
+        table, lens = pool.block_table(S)
+        self._pps = att.default_pages_per_split(len(S), c.kv_heads, table.shape[1], self.n_prefix_pages)
+        self._ws = torch.empty(att.decode_workspace_bytes(len(S), c.q_heads, c.head_dim, table.shape[1],
+                                                          self._pps, self.n_prefix_pages),
+                               dtype=torch.uint8, device=self.device)
+        if c.graphs:
+            # One read-only decode initialises the kernels (and the library's side stream) outside
+            # capture; the decode graph is then captured here, so no step times a capture.
+            kp, vp = pool.layer_pages(0)
+            att.paged_decode(self.qdec[:len(S)], kp, vp, table, lens,
+                             num_prefix_pages=self.n_prefix_pages, pages_per_split=self._pps,
+                             workspace=self._ws)
+            torch.cuda.synchronize(self.device)
+            self._graph = self._capture_decode(S, self._dec_idx)
 
     def _pages(self, n_tokens: int) -> int:
         return (n_tokens + PAGE - 1) // PAGE
@@ -178,8 +194,6 @@ class FusionLoop:
             self._check()
         # decode: one token per session per iteration, every layer
         ones = [1] * len(S)
-        if self._dec_idx is None:
-            self._dec_idx = pool.batch_index(S, ones)
         dec_idx = self._dec_idx
         for _ in range(c.decode_tokens):
             if self._graph is not None:
@@ -197,17 +211,9 @@ class FusionLoop:
                     pool.write_layer(S, start, layer, self.kbuf[:len(S)], self.vbuf[:len(S)], ones,
                                      index=dec_idx)
                     kp, vp = pool.layer_pages(layer)
-                    if self._ws is None:
-                        self._pps = att.default_pages_per_split(len(S), c.kv_heads, table.shape[1],
-                                                                self.n_prefix_pages)
-                        self._ws = torch.empty(att.decode_workspace_bytes(
-                            len(S), c.q_heads, c.head_dim, table.shape[1], self._pps,
-                            self.n_prefix_pages), dtype=torch.uint8, device=self.device)
                     att.paged_decode(self.qdec[:len(S)], kp, vp, table, lens,
                                      num_prefix_pages=self.n_prefix_pages,
                                      pages_per_split=self._pps, workspace=self._ws)
-                if c.graphs:
-                    self._graph = self._capture_decode(S, dec_idx)
             launches += 2 + 4 * c.layers
             own = sum(self._pages(s.current_len) - self.n_prefix_pages for s in S)
             bytes_read += c.layers * (self.n_prefix_pages + own) * self.page_bytes
@@ -227,7 +233,8 @@ class FusionLoop:
     def _capture_decode(self, S, dec_idx) -> dict:
         """One decode iteration of every session as a CUDA graph: pool reserve and block-table
         gather on device buffers, then per layer the K/V append and the paged decode.  Captured
-        after an eager iteration has initialised every kernel; nothing in it allocates."""
+        in setup, after a read-only decode has initialised the decode kernels; nothing in it
+        allocates."""
         c, pool, n = self.cfg, self.pool, len(S)
         i32 = dict(dtype=torch.int32, device=self.device)
         g = {"start": torch.empty(n, **i32), "ones": torch.ones(n, **i32),
