@@ -80,13 +80,18 @@ constexpr uint32_t OFF_V = OFF_K + 2 * kTileBytes;       // 2 stages
 constexpr uint32_t OFF_EPI = OFF_V + 2 * kTileBytes;     // epilogue staging, 4 KB per softmax warp
 constexpr uint32_t kEpiWarpBytes = 4096;
 constexpr uint32_t OFF_BAR = OFF_EPI + 8 * kEpiWarpBytes;
-constexpr uint32_t kSmemBytes = OFF_BAR + 256 + 1024;
+constexpr uint32_t OFF_RESP = OFF_BAR + 256;               // work-ring responses, 16 B each
+constexpr int kRing = 4;                                    // work-ring depth (a power of two)
+constexpr uint32_t kSmemBytes = OFF_RESP + 16 * kRing + 1024;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
 constexpr uint32_t kColS = 0, kColO = 256, kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;
 
 enum Bar { Q_FULL = 0, Q_EMPTY = 1, K_FULL = 2, K_EMPTY = 4, V_FULL = 6, V_EMPTY = 8, S_FULL = 10,
-           P_FULL = 12, O_DONE = 14, P_HALF = 16, NUM_BARS = 18 };
+           P_FULL = 12, O_DONE = 14, P_HALF = 16, ITEM_FULL = 18, ITEM_EMPTY = 22, NUM_BARS = 26 };
+static_assert(8 * NUM_BARS + 16 <= 256, "barriers, abort flag and TMEM slot fit before OFF_RESP");
+// Consumers of a work-ring slot: the producer, the MMA warp and the 8 softmax warps.
+constexpr int kRingConsumers = 10;
 
 enum class Mode { Dense, Paged, Prefix };
 
@@ -211,6 +216,43 @@ __device__ __forceinline__ Item item_coords(const Params& p, int w, int lane) {
     return it;
 }
 
+// Work distribution (all modes): the grid has one CTA per work item, ordered heavy first, and
+// a CTA that has finished its item takes over the item of a CTA that has not been launched yet
+// (cluster launch control: the hardware cancels that CTA's launch and reports its index).  So
+// the first wave of CTAs keeps working until the queue is empty, like a persistent kernel, but
+// with dynamic load balance: ragged items (paged prefill) no longer leave SMs idle at the end.
+// The producer requests the next item one item ahead; every role reads the answer from a ring
+// of kRing slots in shared memory (mbarrier-signalled) and releases the slot after reading it.
+__device__ __forceinline__ void clc_try_cancel(uint32_t resp, uint32_t bar) {
+    asm volatile(
+        "clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 "
+        "[%0], [%1];" ::"r"(resp),
+        "r"(bar)
+        : "memory");
+}
+// The item index a response names, or -1 when no launch was cancelled (no work left).
+__device__ __forceinline__ int clc_item(uint32_t resp) {
+    uint32_t cancelled;
+    asm volatile(
+        "{\n\t.reg .b128 h;\n\t.reg .pred p;\n\t"
+        "ld.shared.b128 h, [%1];\n\t"
+        "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, h;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(cancelled)
+        : "r"(resp)
+        : "memory");
+    if (!cancelled) return -1;
+    uint32_t x;
+    asm volatile(
+        "{\n\t.reg .b128 h;\n\t"
+        "ld.shared.b128 h, [%1];\n\t"
+        "clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %0, h;\n\t}"
+        : "=r"(x)
+        : "r"(resp)
+        : "memory");
+    return static_cast<int>(x);
+}
+
 // HDIM: head_dim, 128 or 64.  At 64 a tile is a single 128-byte-swizzled [rows][64] box and the
 // MMAs run with K = 64 (QK^T) and N = 64 (P.V).
 template <Mode M, int HDIM>
@@ -243,6 +285,10 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
             mbar_init(bar(P_HALF + s), 4);
             mbar_init(bar(O_DONE + s), 1);
         }
+        for (int r = 0; r < kRing; ++r) {
+            mbar_init(bar(ITEM_FULL + r), 1);
+            mbar_init(bar(ITEM_EMPTY + r), kRingConsumers);
+        }
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -254,6 +300,18 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    auto resp = [&](int r) { return sbase + OFF_RESP + 16u * r; };
+    // Item k >= 1 of this CTA (all 32 lanes call it): -1 when the queue is empty or a wait gave
+    // up (then ok is false).
+    auto next_item = [&](int k, bool& ok) -> int {
+        const int r = (k - 1) & (kRing - 1);
+        ok = __all_sync(0xffffffffu, mbar_wait(bar(ITEM_FULL + r), ((k - 1) / kRing) & 1, abort_flag, 14));
+        if (!ok) return -1;
+        const int w = clc_item(resp(r));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(ITEM_EMPTY + r));
+        return w;
+    };
 
     // Registers move from warpgroup 0 (TMA, MMA and two idle warps) to the two softmax
     // warpgroups, whose whole-row S registers otherwise spill: 128 x 88 + 256 x 208 = 64512, within
@@ -269,9 +327,20 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
             tma_prefetch_desc(&tmk);
             tma_prefetch_desc(&tmv);
         }
-        int g = 0, qi = 0;
+        int g = 0, qi = 0, requested = 0;
         bool ok = true;
-        for (int w = blockIdx.x; w < p.n_items && ok; w += gridDim.x) {
+        for (int k = 0, w = blockIdx.x; ok && w >= 0 && w < p.n_items; w = next_item(++k, ok)) {
+            // ask for the item after this one (a request follows only a successful answer)
+            if (lane == 0) {
+                const int r = k & (kRing - 1);
+                if (k >= kRing) ok = mbar_wait(bar(ITEM_EMPTY + r), ((k / kRing) - 1) & 1, abort_flag, 15);
+                if (ok) {
+                    mbar_arrive_expect_tx(bar(ITEM_FULL + r), 16);
+                    clc_try_cancel(resp(r), bar(ITEM_FULL + r));
+                    requested = k + 1;
+                }
+            }
+            if (!(ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0)) break;
             // Paged modes: a 128-key tile is 8 pages x (HD / 64) boxes of [16 rows][64 dims].
             // Lane 2 * page + half issues one box of K and one of V, so the whole tile's boxes go
             // out at once; its page id is fetched one block ahead.  Prefix mode reads the first
@@ -422,6 +491,17 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
             }
             if (ok && qi > 0) mbar_wait(bar(Q_EMPTY), (qi - 1) & 1, abort_flag, 13);
         }
+        // The answer to the last request must land before the CTA exits (it is normally read
+        // already; after a give-up it may still be in flight).
+        if (lane == 0 && requested > 0) {
+            const int r = (requested - 1) & (kRing - 1);
+            const uint32_t par = ((requested - 1) / kRing) & 1;
+            if (!mbar_try_wait(bar(ITEM_FULL + r), par)) {
+                const uint64_t t0 = global_timer_ns();
+                while (!mbar_try_wait(bar(ITEM_FULL + r), par) && global_timer_ns() - t0 < 100000000ull) {
+                }
+            }
+        }
         __syncwarp();
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
@@ -455,7 +535,7 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
         auto vote = [&](bool v) { return __all_sync(0xffffffffu, v); };
         int g = 0, qi = 0, pc[2] = {0, 0};
         bool ok = true;
-        for (int w = blockIdx.x; w < p.n_items && ok; w += gridDim.x) {
+        for (int k = 0, w = blockIdx.x; ok && w >= 0 && w < p.n_items; w = next_item(++k, ok)) {
             const Item it = item_coords<M>(p, w, lane);
             if (it.nbk == 0) {
                 if constexpr (M == Mode::Prefix) {
@@ -550,7 +630,9 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
         int cnt = 0;        // blocks this tile has processed, across items
         int ocnt = 0;       // items with blocks this tile has finished (O_DONE phases)
         bool ok = true;
-        for (int w = blockIdx.x; w < p.n_items && ok; w += gridDim.x) {
+        // The next item is fetched at the end of the body: fetching it at the top keeps one more
+        // value live across the loop and made these warps spill.
+        for (int k = 1, w = blockIdx.x; ok && w >= 0 && w < p.n_items; w = next_item(k++, ok)) {
             const Item it = item_coords<M>(p, w, lane);
             const int n_blk = it.nb[t];
             int qpos = 0, key_limit = 0, n = 0;

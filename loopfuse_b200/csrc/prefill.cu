@@ -33,13 +33,6 @@ int set_smem_attr() {
     return LF_OK;
 }
 
-int sm_count(int* sms) {
-    int dev = 0;
-    LF_CHECK_CUDA(cudaGetDevice(&dev));
-    LF_CHECK_CUDA(cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, dev));
-    return LF_OK;
-}
-
 template <int HD>
 int launch_dense(const lf_bf16* q, const lf_bf16* k, const lf_bf16* v, lf::tc2::Params p,
                  long n_items, cudaStream_t st) {
@@ -59,11 +52,10 @@ int launch_dense(const lf_bf16* q, const lf_bf16* k, const lf_bf16* v, lf::tc2::
     if (rc) return rc;
     rc = set_smem_attr<Mode::Dense, HD>();
     if (rc) return rc;
-    int sms = 0;
-    rc = sm_count(&sms);
-    if (rc) return rc;
-    const long grid = n_items < sms ? n_items : sms;   // persistent: one CTA per SM
-    attn2_kernel<Mode::Dense, HD><<<(unsigned)grid, kThreads, kSmemBytes, st>>>(mq, mk, mv, p);
+    // One CTA per item: CTAs of the first wave take over the items of CTAs not yet launched
+    // (cluster launch control), so the grid behaves like a persistent one with dynamic balance.
+    LF_CHECK_ARG(n_items <= 2147483647L, "prefill: too many work items");
+    attn2_kernel<Mode::Dense, HD><<<(unsigned)n_items, kThreads, kSmemBytes, st>>>(mq, mk, mv, p);
     return lf::launch_status("prefill");
 }
 
@@ -88,11 +80,8 @@ int launch_paged(const lf_bf16* q, const lf_bf16* kp, const lf_bf16* vp, int tot
     if (rc) return rc;
     rc = set_smem_attr<Mode::Paged, HD>();
     if (rc) return rc;
-    int sms = 0;
-    rc = sm_count(&sms);
-    if (rc) return rc;
-    const long grid = n_items < sms ? n_items : sms;
-    attn2_kernel<Mode::Paged, HD><<<(unsigned)grid, kThreads, kSmemBytes, st>>>(mq, mk, mv, p);
+    LF_CHECK_ARG(n_items <= 2147483647L, "prefill paged: too many work items");
+    attn2_kernel<Mode::Paged, HD><<<(unsigned)n_items, kThreads, kSmemBytes, st>>>(mq, mk, mv, p);
     return lf::launch_status("prefill paged");
 }
 
@@ -230,11 +219,7 @@ int launch_prefix_tc(const uint16_t* q, const uint16_t* kp, const uint16_t* vp, 
     const long n_items = (long)p.n_qtiles * Hkv * p.n_chunks;
     LF_CHECK_ARG(n_items < 2147483647L, "decode prefix: too many work items");
     p.n_items = (int)n_items;
-    int sms = 0;
-    rc = sm_count(&sms);
-    if (rc) return rc;
-    const long grid = n_items < sms ? n_items : sms;
-    attn2_kernel<Mode::Prefix, 128><<<(unsigned)grid, kThreads, kSmemBytes, st>>>(mq, mk, mv, p);
+    attn2_kernel<Mode::Prefix, 128><<<(unsigned)n_items, kThreads, kSmemBytes, st>>>(mq, mk, mv, p);
     return launch_status("decode prefix (tensor cores)");
 }
 

@@ -24,6 +24,19 @@ from . import attention as att
 from .workloads import decode_bytes, decode_inputs, prefill_flops, prefill_inputs
 
 
+def _event_ms(fn, reps: int) -> float:
+    """CUDA-event time per call of ``reps`` back-to-back calls of ``fn`` (after one warm-up call
+    by the caller); each call is one launch, so a profiler can skip the warm-up and take some."""
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(max(1, reps)):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / max(1, reps)
+
+
 def run_decode(sessions: int, reps: int, pps: int) -> None:
     w = decode_inputs(N=sessions, seed=0)
     max_pages = w.block_table.shape[1]
@@ -92,10 +105,10 @@ def run_fusion_decode(sessions: int, reps: int, pps: int, private: int, layers: 
 
 def run_prefill(batch: int, seq: int, reps: int) -> None:
     q, k, v = prefill_inputs(batch, 32, 8, seq, 128, seed=0)
-    for _ in range(1 + reps):
-        att.prefill_attention_fwd(q, k, v, causal=True)
-    torch.cuda.synchronize()
-    print(f"prefill B={batch} S={seq} flops={prefill_flops(batch, 32, seq, 128):.4e}")
+    att.prefill_attention_fwd(q, k, v, causal=True)
+    ms = _event_ms(lambda: att.prefill_attention_fwd(q, k, v, causal=True), reps)
+    fl = prefill_flops(batch, 32, seq, 128)
+    print(f"prefill B={batch} S={seq} flops={fl:.4e} ms_per_call={ms:.4f} TFLOPs={fl / ms / 1e9:.1f}")
 
 
 def run_pool(reps: int) -> None:
@@ -136,11 +149,11 @@ def run_paged(sessions: int, reps: int) -> None:
     table, sl = pool.block_table(ss)
     cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32, device="cuda")
     kp, vp = pool.layer_pages(0)
-    for _ in range(1 + reps):
-        att.prefill_paged(q, kp, vp, table, cu, sl, max(lens))
-    torch.cuda.synchronize()
+    att.prefill_paged(q, kp, vp, table, cu, sl, max(lens))
+    ms = _event_ms(lambda: att.prefill_paged(q, kp, vp, table, cu, sl, max(lens)), reps)
     fl = sum(4 * 128 * 32 * n * 4096 + 4 * 128 * 32 * n * (n + 1) // 2 for n in lens)
-    print(f"paged prefill sessions={sessions} new_tokens={T} flops={fl:.4e}")
+    print(f"paged prefill sessions={sessions} new_tokens={T} flops={fl:.4e} ms_per_call={ms:.4f} "
+          f"TFLOPs={fl / ms / 1e9:.1f}")
 
 
 def run_epilogue(tokens: int, reps: int) -> None:
