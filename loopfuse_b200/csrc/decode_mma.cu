@@ -130,6 +130,9 @@ split_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
     __syncwarp();
 
     int ids = 0, ids_batch = -1;                   // page ids of 32 pages, one per lane
+    // A session's own pages are read once: evicted first from L2, so the split and prefix
+    // partials that the combine reads next stay there.
+    const uint64_t l2_policy = sm100::l2_evict_first_policy();
     auto issue = [&](int k) {                      // warp-uniform
         if (k >= my_pages) return;
         const int b = k >> 5;
@@ -148,8 +151,9 @@ split_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
             sm100::mbar_arrive_expect_tx(bar, LY::kStageBytes);
 #pragma unroll
             for (int bx = 0; bx < D / 64; ++bx) {
-                sm100::tma_load_3d(dst + bx * 2048, &tmk, bar, 64 * bx, 0, row);
-                sm100::tma_load_3d(dst + LY::kHeadPageBytes + bx * 2048, &tmv, bar, 64 * bx, 0, row);
+                sm100::tma_load_3d_hint(dst + bx * 2048, &tmk, bar, 64 * bx, 0, row, l2_policy);
+                sm100::tma_load_3d_hint(dst + LY::kHeadPageBytes + bx * 2048, &tmv, bar, 64 * bx, 0,
+                                        row, l2_policy);
             }
         }
     };
