@@ -155,14 +155,17 @@ inline int suffix_splits(int max_pages, int pps, int n_prefix) {
 // tiles, KV head, chunk).  Longer chunks amortise an item's fixed cost (start-up loads, epilogue)
 // and leave fewer partials for the combine; shorter ones make more items, which matters when the
 // prefix pass is the critical path (few sessions, short private runs).  The chunk starts at 32
-// pages and doubles while the pass keeps at least 64 items.  Measured on B200 with a 4096-token
-// prefix and 600-1600 private tokens per session: 64 sessions -> 32 pages, 96-128 -> 64,
-// 256 -> 128, 512 -> 256, each the fastest of 16..256 pages or within 3% of it.
+// pages and doubles while the pass keeps at least 8 items per KV head (64 at 8 KV heads).
+// Measured on B200 with a 4096-token prefix and 600-1600 private tokens per session: 64
+// sessions -> 32 pages, 96-128 -> 64, 256 -> 128, 512 -> 256, each the fastest of 16..256 pages
+// or within 3% of it.  Counting per KV head makes the chunk -- and with it the order in which
+// partials are merged -- depend on the sessions only, not on how many KV heads one call holds:
+// a head-parallel decode over a share of the heads reproduces the one-GPU result bit for bit.
 constexpr int kMinPrefixChunk = 32;
-inline int prefix_chunk_pages(int N, int G, int Hkv, int n_prefix) {
+inline int prefix_chunk_pages(int N, int G, int n_prefix) {
     const long tiles = ((long)N * G + 255) / 256;
     int c = kMinPrefixChunk;
-    while (c < n_prefix && tiles * Hkv * ((n_prefix + 2L * c - 1) / (2L * c)) >= 64) c *= 2;
+    while (c < n_prefix && tiles * ((n_prefix + 2L * c - 1) / (2L * c)) >= 8) c *= 2;
     return c;
 }
 inline int prefix_chunks(int chunk_pages, int n_prefix) {
@@ -326,7 +329,7 @@ static int decode_impl(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* 
 
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int G = num_q_heads / num_kv_heads;
-    const int chunk = decode::prefix_chunk_pages(num_seqs, G, num_kv_heads, num_prefix_pages);
+    const int chunk = decode::prefix_chunk_pages(num_seqs, G, num_prefix_pages);
     const int n_slots = decode::num_slots(max_pages, pages_per_split, num_prefix_pages, chunk);
     const int max_split = decode::suffix_splits(max_pages, pages_per_split, num_prefix_pages);
     const int n_prefix_chunks = decode::prefix_chunks(chunk, num_prefix_pages);
@@ -550,8 +553,7 @@ extern "C" int lf_decode_fwd_noalloc(const lf_bf16* q, const lf_bf16* k_pages,
     int rc = decode::device_sm_count(&sms);
     if (rc != LF_OK) return rc;
     int pps = decode::default_split(num_seqs, num_kv_heads, max_pages, num_prefix_pages, sms);
-    const int chunk = decode::prefix_chunk_pages(num_seqs, num_q_heads / num_kv_heads, num_kv_heads,
-                                                 num_prefix_pages);
+    const int chunk = decode::prefix_chunk_pages(num_seqs, num_q_heads / num_kv_heads, num_prefix_pages);
     while (decode::partial_bytes(num_seqs, num_q_heads, head_dim, max_pages, pps, num_prefix_pages,
                                  chunk) >
                (size_t)LF_DECODE_NOALLOC_SCRATCH_BYTES &&
