@@ -116,3 +116,46 @@ def test_paged_prefill_sessions_without_new_tokens():
         d = (o[off:off + n].permute(1, 0, 2).unsqueeze(0).float().cpu() - ref).abs()
         assert d.max().item() <= TOL_MAX and d.mean().item() <= TOL_MEAN
         off += n
+
+
+def test_paged_prefill_many_ragged_items_fp32():
+    """Agent-shaped appends with far more work items than SMs: 96 sessions forked from a
+    1024-token prefix, 1-300 new tokens each (3840 items, most CTAs take over pending ones).
+    Every session and KV head against the fp32 GPU reference; a second launch must give the
+    same bits (an item is computed whole by whichever CTA takes it)."""
+    from fp32_gpu_reference import prefill_unit
+    g = torch.Generator(device="cuda").manual_seed(21)
+    gc = torch.Generator().manual_seed(21)
+    N, hq, hkv, D, L = 96, 32, 8, 128, 1
+    counts = [int(x) for x in torch.randint(1, 301, (N,), generator=gc)]
+    pool = KVPool(num_layers=L, num_heads=hq, num_kv_heads=hkv, head_dim=D, max_seq_len=1400,
+                  max_slots=N + 1, dtype=torch.bfloat16)
+    root = pool.allocate_slot()
+    pre = _rand(L, 1024, hkv, D, g=g)
+    pool.append([root], [pre], [pre * 0.5])
+    states = pool.fork(root, 1024, n=N)
+    start = pool.reserve(states, counts)
+    T = sum(counts)
+    pool.write_layer(states, start, 0, _rand(T, hkv, D, g=g), _rand(T, hkv, D, g=g), counts)
+    q = _rand(T, hq, D, g=g)
+    table, lens = pool.block_table(states)
+    cu = torch.tensor([0] + list(torch.tensor(counts).cumsum(0)), dtype=torch.int32, device="cuda")
+    kp, vp = pool.layer_pages(0)
+    o = att.prefill_paged(q, kp, vp, table, cu, lens, max(counts))
+    again = att.prefill_paged(q, kp, vp, table, cu, lens, max(counts))
+    assert torch.equal(o, again)
+    G = hq // hkv
+    worst, total, cnt = 0.0, 0.0, 0
+    off = 0
+    for i, s in enumerate(states):
+        n = counts[i]
+        k, v = pool.read(s, 0)                                # [Hkv, Lk, D]
+        for h in range(hkv):
+            qi = q[off:off + n, h * G:(h + 1) * G].permute(1, 0, 2)        # [G, n, D]
+            ref, _ = prefill_unit(qi, k[h], v[h], causal=True)
+            d = (o[off:off + n, h * G:(h + 1) * G].permute(1, 0, 2).float() - ref).abs()
+            worst = max(worst, d.max().item())
+            total += d.sum().item()
+            cnt += d.numel()
+        off += n
+    assert worst <= TOL_MAX and total / cnt <= TOL_MEAN, (worst, total / cnt)
