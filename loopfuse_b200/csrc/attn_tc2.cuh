@@ -1,8 +1,9 @@
-// tcgen05 attention core: persistent CTAs, two query tiles per work item ("ping-pong").
+// tcgen05 attention core: two query tiles per work item ("ping-pong"), dynamic work list.
 //
-// One CTA runs on each SM and walks a static list of work items (CTA c takes items c, c+G,
-// c+2G, ... of a heavy-first order).  An item is two 128-row query tiles that share one K/V
-// stream.  While the softmax warpgroup of one tile works on its scores, the tensor core runs
+// The grid has one CTA per work item, items in heavy-first order.  The first wave of CTAs (one
+// per SM) keeps running: a CTA that finishes an item takes over the item of a CTA not launched
+// yet (cluster launch control, below), so the SMs drain one shared queue.  An item is two
+// 128-row query tiles that share one K/V stream.  While the softmax warpgroup of one tile works on its scores, the tensor core runs
 // the other tile's QK^T and P.V, and the next item's Q/K loads and first QK^T overlap the
 // previous item's epilogue.
 //

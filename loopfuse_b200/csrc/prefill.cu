@@ -3,8 +3,9 @@
 // Replaces prefill_attention_fwd (kernels/triton/prefill_attn.py:127-168, an FA2-style
 // Triton kernel, MHA/fp16 only) and the reference's sm_80 agent_prefill_kernel
 // (kernels/cuda/async_prefill.cu:56-236, wmma QK^T only, no softmax or P.V).  The kernel is the
-// dense instantiation of the tcgen05 attention core in attn_tc2.cuh: persistent CTAs (one per
-// SM) walk pairs of adjacent 128-row query tiles of one (batch, query head), heavy pairs first.
+// dense instantiation of the tcgen05 attention core in attn_tc2.cuh: CTAs that stay resident
+// (one per SM) take pairs of adjacent 128-row query tiles of one (batch, query head) from a
+// heavy-first queue.
 //
 // This file also launches the core's Prefix instantiation for the decode's shared-prefix pass.
 #include <atomic>
