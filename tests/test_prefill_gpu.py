@@ -81,3 +81,40 @@ def test_prefill_reference_api_shape_and_dtype_checks():
         att.prefill_attention_fwd(q.float(), k, v)
     with pytest.raises(RuntimeError):
         att.prefill_attention_fwd(q, k[:, :, :, :64].contiguous(), v)
+
+
+def test_prefill_work_distribution_in_graphs_and_concurrent_streams():
+    """The work list is distributed by the hardware per launch (a CTA that finishes takes over a
+    pending CTA's item), with no counters shared between launches.  So a launch replayed from a
+    CUDA graph, and two launches running at the same time on two streams, must give the bits of
+    a lone eager launch.  Both shapes have several times more items than SMs."""
+    qa, ka, va = prefill_inputs(4, 32, 8, 2048, 128, seed=3)
+    qb, kb, vb = prefill_inputs(2, 16, 4, 4096, 128, seed=4)
+    ref_a = att.prefill_attention_fwd(qa, ka, va, causal=True)
+    ref_b = att.prefill_attention_fwd(qb, kb, vb, causal=True)
+    torch.cuda.synchronize()
+    # graph replays
+    out_a = torch.empty_like(qa)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph):
+            out_a.copy_(att.prefill_attention_fwd(qa, ka, va, causal=True))
+    torch.cuda.current_stream().wait_stream(side)
+    for _ in range(3):
+        out_a.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out_a, ref_a)
+    # two streams at once, several rounds
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    for _ in range(3):
+        s1.wait_stream(torch.cuda.current_stream())
+        s2.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s1):
+            o1 = att.prefill_attention_fwd(qa, ka, va, causal=True)
+        with torch.cuda.stream(s2):
+            o2 = att.prefill_attention_fwd(qb, kb, vb, causal=True)
+        torch.cuda.synchronize()
+        assert torch.equal(o1, ref_a) and torch.equal(o2, ref_b)
