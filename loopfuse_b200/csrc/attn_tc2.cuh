@@ -97,10 +97,13 @@ constexpr int kRingConsumers = 10;
 enum class Mode { Dense, Paged, Prefix };
 
 // Which exp2 pairs of each group of 8 run as a polynomial on the FMA pipe (bit i: pair i % 8);
-// the rest use the MUFU unit.  Two in eight measured best for the dense prefill (A/B over 1/8 to
-// 4/8).  Every mode uses the same share, so a paged prefill over a contiguous context gives the
-// dense prefill's bits.
-constexpr unsigned kPolyMask = 0x88u;
+// the rest use the MUFU unit.  A/B on one box: two in eight is best for the dense prefill (over
+// 1/8 to 4/8), one in eight for paged appends (962 against 933 TFLOP/s at 2/8).  Which pair of
+// the eight matters only to register allocation: pair 3 compiles without spills, pair 7 spills.
+// A paged prefill over a contiguous context therefore differs from the dense prefill in the
+// last bits of some probabilities.
+template <Mode M>
+constexpr unsigned poly_mask() { return M == Mode::Paged ? 0x08u : 0x88u; }
 
 struct Params {
     float c;
@@ -709,7 +712,7 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                 }
                 // exp2, row sum and bf16 P, packed in place: pair i (columns 2i, 2i+1) becomes
                 // r[i], so P of score columns [0, 128) lands in TMEM columns [0, 64) of this
-                // S buffer.  The pairs kPolyMask selects run on the FMA pipe.  The first half
+                // S buffer.  The pairs poly_mask<M>() selects run on the FMA pipe.  The first half
                 // of P is stored and signalled (P_HALF) before the second half is computed, so
                 // its P.V overlaps the rest of this softmax.
                 const uint64_t c2 = f2_pack(p.c, p.c), nm2 = f2_pack(-m_use, -m_use);
@@ -718,7 +721,7 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                     const uint64_t a = ffma2(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])),
                                              c2, nm2);
                     float2 e;
-                    if ((kPolyMask >> (i & 7)) & 1u) {
+                    if ((poly_mask<M>() >> (i & 7)) & 1u) {
                         e = exp2_poly2(a);
                     } else {
                         const float2 av = f2_unpack(a);

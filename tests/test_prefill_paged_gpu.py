@@ -83,7 +83,11 @@ def test_paged_prefill_equals_dense_prefill_on_contiguous_context():
     od = att.prefill_attention_fwd(q.permute(1, 0, 2).unsqueeze(0).contiguous(),
                                    k[0].permute(1, 0, 2).unsqueeze(0).contiguous(),
                                    v[0].permute(1, 0, 2).unsqueeze(0).contiguous())
-    assert torch.equal(o.permute(1, 0, 2), od[0])
+    # The two modes share the tile loop but not the exp2 split between MUFU and FMA, so some
+    # bf16 outputs differ by a rounding step; a paging error would be far larger.
+    d = (o.permute(1, 0, 2).float() - od[0].float()).abs()
+    same, worst, mean = (d == 0).float().mean().item(), d.max().item(), d.mean().item()
+    assert same >= 0.9 and worst <= 5e-3 and mean <= 1e-4, (same, worst, mean)
 
 
 def test_paged_prefill_sessions_without_new_tokens():
