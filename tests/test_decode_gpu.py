@@ -63,6 +63,24 @@ def test_decode_shared_prefix(prefix_tokens):
     _check(o_ns, ref, "no sharing")
 
 
+@pytest.mark.parametrize("hq,hkv,d", [(12, 12, 64), (16, 4, 64), (8, 2, 64), (16, 2, 64),
+                                      (16, 4, 128), (8, 8, 128)])
+@pytest.mark.parametrize("prefix_tokens", [160, 2048])
+def test_decode_shared_prefix_head_shapes(hq, hkv, d, prefix_tokens):
+    """The shared-prefix pass for every GQA group size and both head dims: head_dim 64 runs the
+    CUDA-core prefix kernel, 128 the tensor-core one; both write bf16 O / l partials that the
+    combine scales back.  The workspace is filled with NaN bytes first."""
+    lengths = [1, 20, 160, 700, 2048, 2049, 3000, 31, 4000, 16, 2100]
+    w = decode_inputs(N=len(lengths), Hq=hq, Hkv=hkv, D=d, lengths=lengths,
+                      prefix_tokens=prefix_tokens, seed=hq + hkv + d)
+    max_pages = w.block_table.shape[1]
+    need = att.decode_workspace_bytes(len(lengths), hq, d, max_pages, 8, w.n_prefix_pages)
+    ws = torch.full((need,), 255, dtype=torch.uint8, device="cuda")
+    o = att.paged_decode(w.q, w.k_pages, w.v_pages, w.block_table, w.seq_lens,
+                         num_prefix_pages=w.n_prefix_pages, pages_per_split=8, workspace=ws)
+    _check(o, _oracle(w)[0], f"hq={hq} hkv={hkv} d={d} prefix={prefix_tokens}")
+
+
 def test_decode_reference_api_matches_reference_check():
     """decode_attention_fwd on [B,H,S,D] vs the reference's _reference_decode_attn (fp32 here)."""
     g = torch.Generator(device="cuda").manual_seed(7)
