@@ -50,7 +50,7 @@
 //                     one chunk of shared-prefix pages; q via 4-D TMA boxes over [N][Hkv][G][D];
 //                     K/V pages [P][Hkv][16][D] via 16-row boxes through the block table of the
 //                     item's longest session (pages past the run read zeros); epilogue writes
-//                     fp32 partials (o, max, sum) into the decode workspace.
+//                     partials into the decode workspace: O / l as bf16, (max, sum) as fp32.
 //
 // Every mbarrier wait is bounded in time; a timeout aborts all roles, frees TMEM and leaves a
 // code that lf_device_status() reports.
