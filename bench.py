@@ -364,8 +364,8 @@ def run_agent(args):
     grp.close()
 
 
-# --------------------------------------------------------------------------- parity checker
-# north_star tolerance for bf16 outputs against fp32 attention
+# --------------------------------------------------------------------------- parity check
+# parity tolerance for bf16 outputs against fp32 attention
 TOL_MAX, TOL_MEAN = 2e-2, 2e-3
 
 
@@ -542,7 +542,7 @@ def main():
 
     # ---------------- parity at full size (outside every timed region) ----------------
     parity = {"tolerance": {"max_abs": TOL_MAX, "mean_abs": TOL_MEAN},
-              "checker": "fp32 attention on the GPU (TF32 off), every unit"}
+              "against": "fp32 attention on the GPU (TF32 off), every unit"}
     if not args.no_parity:
         step()
         torch.cuda.synchronize()

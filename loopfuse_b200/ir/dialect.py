@@ -8,7 +8,7 @@ annotates them identically.  The op classes carry only what the hot path and
 its tests use: operands, results, ``phase``, ``target``, ``attrs`` and
 ``metadata``.
 
-Added for this build: ``num_kv_heads`` on ``KVCacheType`` (defaults to
+Added here: ``num_kv_heads`` on ``KVCacheType`` (defaults to
 ``num_heads``, so existing callers are unchanged) and the Llama-3-8B configs
 used by the B200 workloads.
 """
@@ -31,7 +31,7 @@ class Phase(Enum):
 
 
 class KernelTarget(Enum):
-    """Backend a program is compiled for.  Only CUDA executes in this build."""
+    """Backend a program is compiled for.  Only CUDA executes in this package."""
     TRITON = "triton"
     CUDA = "cuda"
     PALLAS = "pallas"

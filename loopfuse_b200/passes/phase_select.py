@@ -7,7 +7,7 @@ is what the names *resolve to*: ``resolve_kernel`` maps the CUDA entries,
 ``kernels.cuda.async_prefill/agent_prefill_kernel`` and
 ``kernels.cuda.ring_kv_cache/ring_kv_decode_kernel``, onto this package's
 sm_100a prefill and paged decode.  TRITON and PALLAS names stay selectable
-(annotation only) but do not execute: this build has one backend and no CPU
+(annotation only) but do not execute: this package has one backend and no CPU
 fallback, and the EAGER entry is the test oracle, not a runtime path.
 
 The roofline classification (``:130-144``) is kept with the reference's

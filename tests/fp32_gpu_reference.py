@@ -1,10 +1,10 @@
-"""fp32 attention computed on the GPU (TF32 off): the checker for full-size parity tests.
+"""fp32 attention on the GPU (TF32 off): the reference computation of full-size parity tests.
 
 The CPU oracle (``oracle/attention.py``) states the semantics and is checked against the
 reference's fixtures; at the full sizes of the benchmark workloads (8 x 32 x 4096 x 4096 prefill
 scores, 256 sessions of up to 32768 tokens) it would take minutes on the host, so these
 functions compute the same fp32 math with torch on the device, one unit at a time.  They are
-test checkers: nothing in the package calls them.
+test references: nothing in the package calls them.
 """
 from __future__ import annotations
 

@@ -3,7 +3,7 @@
 Fixtures come from ``tests/golden/make_golden.py`` (imports the reference):
 ``_reference_decode_attn`` outputs and the fp32 SDPA causal check of the
 reference's prefill verifier.  These pin the oracle before it is trusted as
-the checker for the sm_100a kernels.
+the reference computation of the sm_100a kernels' parity tests.
 """
 import os
 
