@@ -148,3 +148,28 @@ def test_decode_sessions_shorter_than_the_prefix(lengths):
     o = att.paged_decode(w.q, w.k_pages, w.v_pages, w.block_table, w.seq_lens,
                          num_prefix_pages=w.n_prefix_pages, pages_per_split=8, workspace=ws)
     _check(o, _oracle(w)[0], f"lengths={lengths}")
+
+
+@pytest.mark.parametrize("hq,hkv,d", [(32, 8, 128), (16, 4, 64)])
+@pytest.mark.parametrize("prefix_tokens", [0, 1024])
+def test_decode_empty_sessions(hq, hkv, d, prefix_tokens):
+    """Sessions with no tokens yet (length 0, a table row of -1) beside others in one batch: their
+    output rows are zeros and their LSE is -inf (attention over no keys is an empty sum), and the
+    other sessions match the oracle.  The workspace is NaN-filled, so a read of a partial slot
+    that nothing wrote would show."""
+    lengths = [0, 1, 300, 0, 2049, 1100, 0]
+    w = decode_inputs(N=len(lengths), Hq=hq, Hkv=hkv, D=d, lengths=lengths,
+                      prefix_tokens=prefix_tokens, seed=12)
+    max_pages, pps = w.block_table.shape[1], 8
+    need = att.decode_workspace_bytes(len(lengths), hq, d, max_pages, pps, w.n_prefix_pages)
+    ws = torch.full((need,), 255, dtype=torch.uint8, device="cuda")
+    o, lse = att.paged_decode(w.q, w.k_pages, w.v_pages, w.block_table, w.seq_lens,
+                              num_prefix_pages=w.n_prefix_pages, pages_per_split=pps, workspace=ws,
+                              return_lse=True)
+    empty = [i for i, L in enumerate(lengths) if L == 0]
+    rest = [i for i, L in enumerate(lengths) if L > 0]
+    assert torch.count_nonzero(o[empty]).item() == 0
+    assert torch.isneginf(lse[empty]).all()
+    ref, ref_lse = _oracle(w, rest)
+    _check(o[rest], ref, f"hq={hq} hkv={hkv} d={d} prefix={prefix_tokens}")
+    assert (lse[rest].cpu() - ref_lse).abs().max().item() < 1e-2
