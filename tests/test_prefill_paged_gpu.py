@@ -163,3 +163,42 @@ def test_paged_prefill_many_ragged_items_fp32():
             cnt += d.numel()
         off += n
     assert worst <= TOL_MAX and total / cnt <= TOL_MEAN, (worst, total / cnt)
+
+
+def test_paged_prefill_sessions_with_no_new_tokens():
+    """Sessions that append nothing this step (equal cu_seqlens_q entries; one of them has no
+    context either) beside sessions that do: they own no query rows, every row of a NaN-filled
+    output is written, and the other sessions match the oracle."""
+    g = torch.Generator(device="cuda").manual_seed(21)
+    hq, hkv, D = 32, 8, 128
+    pool = KVPool(num_layers=1, num_heads=hq, num_kv_heads=hkv, head_dim=D, max_seq_len=2048,
+                  max_slots=5, dtype=torch.bfloat16)
+    states = [pool.allocate_slot() for _ in range(4)]
+    ctx = [300, 37, 0, 500]
+    for s, n in zip(states, ctx):
+        if n:
+            kk = _rand(1, n, hkv, D, g=g)
+            pool.append([s], [kk], [kk - 0.5])
+    new_counts = [0, 64, 0, 129]
+    start = pool.reserve(states, new_counts)
+    T = sum(new_counts)
+    newk, newv = _rand(T, hkv, D, g=g), _rand(T, hkv, D, g=g)
+    pool.write_layer(states, start, 0, newk, newv, new_counts)
+    q = _rand(T, hq, D, g=g)
+    table, lens = pool.block_table(states)
+    cu = torch.tensor([0] + list(torch.tensor(new_counts).cumsum(0)), dtype=torch.int32, device="cuda")
+    kp, vp = pool.layer_pages(0)
+    o = torch.full_like(q, float("nan"))
+    att.prefill_paged(q, kp, vp, table, cu, lens, max(new_counts), out=o)
+    assert not torch.isnan(o).any()
+    off = 0
+    for i, s in enumerate(states):
+        n = new_counts[i]
+        if n == 0:
+            continue
+        k, v = pool.read(s, 0)
+        qi = q[off:off + n].permute(1, 0, 2).unsqueeze(0)
+        ref, _ = ora.prefill(qi.cpu(), k.unsqueeze(0).cpu(), v.unsqueeze(0).cpu(), causal=True)
+        d = (o[off:off + n].permute(1, 0, 2).unsqueeze(0).float().cpu() - ref).abs()
+        assert d.max().item() <= TOL_MAX and d.mean().item() <= TOL_MEAN, (i, d.max().item())
+        off += n
