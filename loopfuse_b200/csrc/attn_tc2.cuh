@@ -119,6 +119,7 @@ struct Params {
     // G: prefix mode -- the GQA group; paged mode -- query heads packed per work item
     const int32_t* cu_q;     // paged: [N+1] query row offsets
     int max_pairs;           // paged: tile pairs of the longest packed query run
+    int o_align32;           // dense / paged: o is 32-byte aligned (32-byte output stores)
 };
 
 struct Item {
@@ -782,15 +783,29 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                             for (int i = 0; i < 32; ++i) r[i] = 0u;
                         }
                         if (grow < rows) {
-                            uint4* dst = reinterpret_cast<uint4*>(p.o + orow * HD + cc * 32);
+                            // 32-byte stores when o is 32-byte aligned (rows are 2 * HD bytes):
+                            // half the store instructions of 16-byte ones
+                            uint16_t* dst = p.o + orow * HD + cc * 32;
+                            if (p.o_align32) {
 #pragma unroll
-                            for (int v = 0; v < 4; ++v) {
-                                uint4 wv;
-                                wv.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]) * inv, __uint_as_float(r[8 * v + 1]) * inv);
-                                wv.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * inv, __uint_as_float(r[8 * v + 3]) * inv);
-                                wv.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * inv, __uint_as_float(r[8 * v + 5]) * inv);
-                                wv.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * inv, __uint_as_float(r[8 * v + 7]) * inv);
-                                dst[v] = wv;
+                                for (int v = 0; v < 2; ++v) {
+                                    uint32_t w[8];
+#pragma unroll
+                                    for (int i = 0; i < 8; ++i)
+                                        w[i] = pack_bf16x2(__uint_as_float(r[16 * v + 2 * i]) * inv,
+                                                           __uint_as_float(r[16 * v + 2 * i + 1]) * inv);
+                                    st_global_v8(dst + 16 * v, w);
+                                }
+                            } else {
+#pragma unroll
+                                for (int v = 0; v < 4; ++v) {
+                                    uint4 wv;
+                                    wv.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]) * inv, __uint_as_float(r[8 * v + 1]) * inv);
+                                    wv.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * inv, __uint_as_float(r[8 * v + 3]) * inv);
+                                    wv.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * inv, __uint_as_float(r[8 * v + 5]) * inv);
+                                    wv.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * inv, __uint_as_float(r[8 * v + 7]) * inv);
+                                    reinterpret_cast<uint4*>(dst)[v] = wv;
+                                }
                             }
                         }
                     }

@@ -107,6 +107,7 @@ extern "C" int lf_prefill_fwd(const lf_bf16* q, const lf_bf16* k, const lf_bf16*
     Params p{};
     p.c = scale * kLog2e;
     p.o = o;
+    p.o_align32 = (reinterpret_cast<uintptr_t>(o) & 31u) == 0 ? 1 : 0;
     p.lse = lse;
     p.B = batch;
     p.Hq = num_q_heads;
@@ -150,6 +151,7 @@ extern "C" int lf_prefill_paged_fwd(const lf_bf16* q, const lf_bf16* k_pages,
     Params p{};
     p.c = scale * kLog2e;
     p.o = o;
+    p.o_align32 = (reinterpret_cast<uintptr_t>(o) & 31u) == 0 ? 1 : 0;
     p.lse = lse;
     p.Hq = num_q_heads;
     p.Hkv = num_kv_heads;

@@ -52,6 +52,21 @@ def test_prefill_head_dim_64(Sq, Sk, causal):
     _run_and_check(1, 12, 12, Sq, Sk, causal, seed=Sq, D=64)
 
 
+def test_prefill_output_16_byte_aligned():
+    """An output that is 16- but not 32-byte aligned takes the 16-byte store path of the
+    epilogue (32-byte stores otherwise): same bits as the aligned output."""
+    from loopfuse_b200 import _lib
+    q, k, v = prefill_inputs(1, 4, 1, 200, 128, seed=2)
+    o = att.prefill_attention_fwd(q, k, v, causal=True)
+    buf = torch.full((q.numel() + 16,), float("nan"), dtype=torch.bfloat16, device="cuda")
+    o2 = buf[8:8 + q.numel()].view(q.shape)
+    assert o2.data_ptr() % 32 == 16
+    _lib.call("lf_prefill_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), o2.data_ptr(), None,
+              1, 4, 1, 200, 200, 128, 128 ** -0.5, 1, att._stream())
+    torch.cuda.synchronize()
+    assert torch.equal(o2, o)
+
+
 def test_prefill_longer_sequence():
     _run_and_check(1, 8, 2, 1024, 1024, True, seed=11)
 

@@ -191,6 +191,12 @@ def test_paged_prefill_sessions_with_no_new_tokens():
     o = torch.full_like(q, float("nan"))
     att.prefill_paged(q, kp, vp, table, cu, lens, max(new_counts), out=o)
     assert not torch.isnan(o).any()
+    # an output 16- but not 32-byte aligned takes the 16-byte store path: same bits
+    buf = torch.full((q.numel() + 16,), float("nan"), dtype=torch.bfloat16, device="cuda")
+    o16 = buf[8:8 + q.numel()].view(q.shape)
+    assert o16.data_ptr() % 32 == 16
+    att.prefill_paged(q, kp, vp, table, cu, lens, max(new_counts), out=o16)
+    assert torch.equal(o16, o)
     off = 0
     for i, s in enumerate(states):
         n = new_counts[i]
