@@ -120,6 +120,7 @@ struct Params {
     const int32_t* cu_q;     // paged: [N+1] query row offsets
     int max_pairs;           // paged: tile pairs of the longest packed query run
     int o_align32;           // dense / paged: o is 32-byte aligned (32-byte output stores)
+    int part_align32;        // prefix: part_o is 32-byte aligned (32-byte partial stores)
 };
 
 struct Item {
@@ -851,14 +852,30 @@ attn2_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
                         stage[lane * 4 + (v ^ ((lane >> 1) & 3))] = wv;
                     }
                     __syncwarp();
-                    // 64 bytes of a row per 4 lanes, 8 rows per store
+                    if (p.part_align32) {
+                        // 64 bytes of a row per 2 lanes (32-byte stores), 16 rows per store
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int rl = i * 8 + (lane >> 2), q = lane & 3;
-                        const uint4 v = stage[rl * 4 + (q ^ ((rl >> 1) & 3))];
-                        const int rr2 = t * BM + g0 + rl;
-                        if (it.n0 + rr2 / p.G < p.N)
-                            reinterpret_cast<uint4*>(p.part_o + slot_of(rr2) * HD)[cc * 4 + q] = v;
+                        for (int i = 0; i < 2; ++i) {
+                            const int rl = i * 16 + (lane >> 1), hf = lane & 1, sw = (rl >> 1) & 3;
+                            const uint4 a = stage[rl * 4 + ((2 * hf) ^ sw)];
+                            const uint4 b = stage[rl * 4 + ((2 * hf + 1) ^ sw)];
+                            const int rr2 = t * BM + g0 + rl;
+                            if (it.n0 + rr2 / p.G < p.N) {
+                                const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+                                st_global_v8(reinterpret_cast<uint8_t*>(p.part_o + slot_of(rr2) * HD) +
+                                                 cc * 64 + hf * 32, w);
+                            }
+                        }
+                    } else {
+                        // 64 bytes of a row per 4 lanes, 8 rows per store
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int rl = i * 8 + (lane >> 2), q = lane & 3;
+                            const uint4 v = stage[rl * 4 + (q ^ ((rl >> 1) & 3))];
+                            const int rr2 = t * BM + g0 + rl;
+                            if (it.n0 + rr2 / p.G < p.N)
+                                reinterpret_cast<uint4*>(p.part_o + slot_of(rr2) * HD)[cc * 4 + q] = v;
+                        }
                     }
                 }
                 if (n_row < p.N) p.part_ml[slot_of(rr)] = make_float2(m_run, l_run);

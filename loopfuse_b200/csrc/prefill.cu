@@ -208,6 +208,7 @@ int launch_prefix_tc(const uint16_t* q, const uint16_t* kp, const uint16_t* vp, 
     p.bt = bt;
     p.lens = lens;
     p.part_o = po;
+    p.part_align32 = (reinterpret_cast<uintptr_t>(po) & 31u) == 0 ? 1 : 0;
     p.part_ml = pml;
     p.N = N;
     p.G = G;

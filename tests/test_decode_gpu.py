@@ -173,3 +173,21 @@ def test_decode_empty_sessions(hq, hkv, d, prefix_tokens):
     ref, ref_lse = _oracle(w, rest)
     _check(o[rest], ref, f"hq={hq} hkv={hkv} d={d} prefix={prefix_tokens}")
     assert (lse[rest].cpu() - ref_lse).abs().max().item() < 1e-2
+
+
+def test_decode_workspace_16_byte_aligned():
+    """A workspace that is 16- but not 32-byte aligned takes the 16-byte store path of the
+    shared-prefix pass (32-byte stores otherwise): the same bits as an aligned workspace."""
+    lengths = [1, 300, 2049, 5000, 1024, 77, 4100]
+    w = decode_inputs(N=len(lengths), lengths=lengths, prefix_tokens=2048, seed=13)
+    max_pages = w.block_table.shape[1]
+    need = att.decode_workspace_bytes(len(lengths), 32, 128, max_pages, 8, w.n_prefix_pages)
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    buf = torch.empty(need + 32, dtype=torch.uint8, device="cuda")
+    ws16 = buf[16:16 + need]
+    assert ws.data_ptr() % 32 == 0 and ws16.data_ptr() % 32 == 16
+    args = (w.q, w.k_pages, w.v_pages, w.block_table, w.seq_lens)
+    o1 = att.paged_decode(*args, num_prefix_pages=w.n_prefix_pages, pages_per_split=8, workspace=ws)
+    o2 = att.paged_decode(*args, num_prefix_pages=w.n_prefix_pages, pages_per_split=8, workspace=ws16)
+    assert torch.equal(o1, o2)
+    _check(o1, _oracle(w)[0], "aligned workspace")
