@@ -106,8 +106,8 @@ int lf_prefill_paged_fwd(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16
  * block_table [N,max_pages] int32 page ids in token order; seq_lens [N] >= 1;
  * o [N,Hq,D]; lse [N,Hq] (nullable, natural log).  Each session's pages are
  * split into chunks of pages_per_split pages, processed by independent CTAs
- * (GQA group of Hq/Hkv heads per CTA, 128-bit coalesced page reads, warp
- * shuffle reductions) and merged by log-sum-exp.  num_prefix_pages > 0 says
+ * (GQA group of Hq/Hkv heads per CTA, pages staged by TMA, warp-level
+ * tensor-core MMA) and merged by log-sum-exp.  num_prefix_pages > 0 says
  * the first num_prefix_pages block-table entries are the same pages for every
  * session (a forked shared prefix): they are read once per group of sessions
  * instead of once per session.  workspace holds the split partials; its size
@@ -131,6 +131,22 @@ int lf_decode_fwd(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* v_pag
                   int num_seqs, int num_q_heads, int num_kv_heads, int head_dim,
                   int num_pages, int max_pages, int pages_per_split, float scale,
                   void* stream);
+
+/* lf_decode_fwd with the K/V append fused in: replaces ring_kv_write_kernel followed by the
+ * decode (kernels/cuda/ring_kv_cache.cu:69-109, then :120-248).  k_new, v_new [N,Hkv,D] are
+ * each session's newest token, at position seq_lens[n] - 1, whose page the caller has already
+ * reserved in block_table (past the num_prefix_pages shared pages, in a page of the session's
+ * own).  The split CTA that holds that page stores the token's rows into k_pages / v_pages
+ * before loading the page, so the pages are written and the launch sequence is one kernel
+ * shorter than a separate append.  Pages afterwards hold what lf_pool_write_kv would have
+ * written.  A page id of the newest token outside [0, num_pages) stores nothing and is
+ * reported through lf_device_status(). */
+int lf_decode_fwd_append(const lf_bf16* q, lf_bf16* k_pages, lf_bf16* v_pages,
+                         const int32_t* block_table, const int32_t* seq_lens, int num_prefix_pages,
+                         const lf_bf16* k_new, const lf_bf16* v_new, lf_bf16* o, float* lse,
+                         void* workspace, size_t workspace_bytes, int num_seqs, int num_q_heads,
+                         int num_kv_heads, int head_dim, int num_pages, int max_pages,
+                         int pages_per_split, float scale, void* stream);
 
 /* Head-tensor-parallel decode with the all-gather of the outputs fused into the combine
  * step (the reference has no multi-GPU path).  This rank holds num_kv_heads of the model's KV

@@ -54,6 +54,8 @@ _SIGS = {
     "lf_decode_default_split": [c_int, c_int, c_int, c_int, c_int, POINTER(c_int)],
     "lf_decode_fwd": [_P, _P, _P, _P, _P, c_int, _P, _P, _P, c_size_t, c_int, c_int, c_int,
                       c_int, c_int, c_int, c_int, c_float, _P],
+    "lf_decode_fwd_append": [_P, _P, _P, _P, _P, c_int, _P, _P, _P, _P, _P, c_size_t, c_int,
+                             c_int, c_int, c_int, c_int, c_int, c_int, c_float, _P],
     "lf_decode_fwd_noalloc": [_P, _P, _P, _P, _P, c_int, _P, _P, c_int, c_int, c_int, c_int,
                               c_int, c_int, c_float, _P],
     "lf_decode_set_profile_events": [_P, _P],

@@ -130,13 +130,20 @@ def paged_decode(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torch.Tensor,
                  block_table: torch.Tensor, seq_lens: torch.Tensor, num_prefix_pages: int = 0,
                  scale: Optional[float] = None, pages_per_split: Optional[int] = None,
                  out: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None,
-                 return_lse: bool = False):
+                 return_lse: bool = False, k_new: Optional[torch.Tensor] = None,
+                 v_new: Optional[torch.Tensor] = None):
     """One-token attention per session over paged K/V.
 
     ``q [N,Hq,D]``; ``k_pages, v_pages [P,Hkv,16,D]`` (one layer of the pool);
     ``block_table [N,max_pages]`` int32; ``seq_lens [N]`` int32.  With
     ``num_prefix_pages > 0`` the first that many block-table entries must be the
     same pages for all sessions; they are then read once per group of sessions.
+
+    ``k_new, v_new [N,Hkv,D]`` (both or neither): each session's newest token, at position
+    ``seq_lens[i] - 1`` in a page already reserved in ``block_table`` past the shared-prefix
+    pages, is stored into ``k_pages`` / ``v_pages`` by the decode itself before it is attended
+    (``lf_decode_fwd_append``): the pages end up as a separate ``KVPool.write_layer`` would leave
+    them, one kernel launch fewer.
     """
     _require(q, "q")
     _require(k_pages, "k_pages")
@@ -157,6 +164,20 @@ def paged_decode(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torch.Tensor,
         workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
     o = out if out is not None else torch.empty_like(q)
     lse = torch.empty((N, Hq), dtype=torch.float32, device=q.device) if return_lse else None
+    if (k_new is None) != (v_new is None):
+        raise LoopfuseError(_lib.LF_EINVAL, "paged_decode: give both k_new and v_new, or neither")
+    if k_new is not None:
+        for t, n in ((k_new, "k_new"), (v_new, "v_new")):
+            _require(t, n)
+            if tuple(t.shape) != (N, Hkv, D):
+                raise LoopfuseError(_lib.LF_EINVAL, f"{n} must be [N,Hkv,D] = {(N, Hkv, D)}")
+        _lib.call("lf_decode_fwd_append", q.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(),
+                  block_table.data_ptr(), seq_lens.data_ptr(), int(num_prefix_pages),
+                  k_new.data_ptr(), v_new.data_ptr(), o.data_ptr(),
+                  lse.data_ptr() if lse is not None else None, workspace.data_ptr(),
+                  workspace.numel() * workspace.element_size(), N, Hq, Hkv, D, P, max_pages, pps,
+                  scale, _stream())
+        return (o, lse) if return_lse else o
     _lib.call("lf_decode_fwd", q.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(),
               block_table.data_ptr(), seq_lens.data_ptr(), int(num_prefix_pages), o.data_ptr(),
               lse.data_ptr() if lse is not None else None, workspace.data_ptr(),

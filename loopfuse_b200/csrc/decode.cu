@@ -253,7 +253,8 @@ namespace lf { namespace decode {
 int launch_split_mma(dim3 grid, cudaStream_t st, const uint16_t* q, const uint16_t* kp,
                      const uint16_t* vp, const int32_t* bt, const int32_t* lens, float* po,
                      float2* pml, int Hq, int Hkv, int D, int num_pages, int max_pages, int pps,
-                     int first_page, int n_slots, float qscale);
+                     int first_page, int n_slots, float qscale,
+                     const uint16_t* k_new, const uint16_t* v_new);
 }}
 
 // Defined in decode_prefix.cu: shared-prefix partials, one pass over the prefix pages per
@@ -307,7 +308,8 @@ static int decode_impl(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* 
                        const decode::CombineOut& out, float* lse, void* workspace,
                        size_t workspace_bytes, int num_seqs, int num_q_heads, int num_kv_heads,
                        int head_dim, int num_pages, int max_pages, int pages_per_split,
-                       float scale, void* stream) {
+                       float scale, void* stream, const lf_bf16* k_new = nullptr,
+                       const lf_bf16* v_new = nullptr) {
     LF_CHECK_ARG(q && k_pages && v_pages && block_table && seq_lens && workspace,
                  "decode: null pointer argument");
     LF_CHECK_ARG(aligned16(q) && aligned16(k_pages) && aligned16(v_pages) && aligned16(workspace),
@@ -380,7 +382,7 @@ static int decode_impl(const lf_bf16* q, const lf_bf16* k_pages, const lf_bf16* 
         int rc = decode::launch_split_mma(grid, st, q16, k_pages, v_pages, block_table, seq_lens,
                                           po, pml, num_q_heads, num_kv_heads, head_dim, num_pages,
                                           max_pages, pages_per_split, num_prefix_pages, n_slots,
-                                          qscale);
+                                          qscale, k_new, v_new);
         if (rc == LF_OK) rc = launch_status("decode split");
         if (rc != LF_OK) {
             if (overlap) {                                    // keep the fork closed
@@ -416,6 +418,27 @@ extern "C" int lf_decode_fwd(const lf_bf16* q, const lf_bf16* k_pages, const lf_
     return decode_impl(q, k_pages, v_pages, block_table, seq_lens, num_prefix_pages, out, lse,
                        workspace, workspace_bytes, num_seqs, num_q_heads, num_kv_heads, head_dim,
                        num_pages, max_pages, pages_per_split, scale, stream);
+}
+
+extern "C" int lf_decode_fwd_append(const lf_bf16* q, lf_bf16* k_pages, lf_bf16* v_pages,
+                                    const int32_t* block_table, const int32_t* seq_lens,
+                                    int num_prefix_pages, const lf_bf16* k_new,
+                                    const lf_bf16* v_new, lf_bf16* o, float* lse, void* workspace,
+                                    size_t workspace_bytes, int num_seqs, int num_q_heads,
+                                    int num_kv_heads, int head_dim, int num_pages, int max_pages,
+                                    int pages_per_split, float scale, void* stream) {
+    LF_CHECK_ARG(o != nullptr && aligned16(o), "decode append: o must be a 16-byte aligned pointer");
+    LF_CHECK_ARG(k_new != nullptr && v_new != nullptr && aligned16(k_new) && aligned16(v_new),
+                 "decode append: k_new and v_new must be 16-byte aligned pointers");
+    // The newest token of every session must lie in a page of its own (past the shared-prefix
+    // pages), which the split pass reads: a table wide enough to hold own pages is required.
+    LF_CHECK_ARG(max_pages > num_prefix_pages,
+                 "decode append: the newest tokens must lie past the %d shared-prefix pages",
+                 num_prefix_pages);
+    const decode::CombineOut out{o, nullptr, 0, 0, num_q_heads};
+    return decode_impl(q, k_pages, v_pages, block_table, seq_lens, num_prefix_pages, out, lse,
+                       workspace, workspace_bytes, num_seqs, num_q_heads, num_kv_heads, head_dim,
+                       num_pages, max_pages, pages_per_split, scale, stream, k_new, v_new);
 }
 
 extern "C" int lf_decode_fwd_gather(const lf_bf16* q, const lf_bf16* k_pages,
@@ -590,7 +613,8 @@ extern "C" int lf_decode_fwd_noalloc(const lf_bf16* q, const lf_bf16* k_pages,
         dim3 grid(max_split, num_kv_heads, num_seqs);
         rc = decode::launch_split_mma(grid, st, q, k_pages, v_pages, block_table, seq_lens, po,
                                       pml, num_q_heads, num_kv_heads, head_dim, num_pages,
-                                      max_pages, pps, num_prefix_pages, n_slots, qscale);
+                                      max_pages, pps, num_prefix_pages, n_slots, qscale, nullptr,
+                                      nullptr);
         if (rc != LF_OK) return rc;
         rc = launch_status("decode noalloc split");
         if (rc != LF_OK) return rc;

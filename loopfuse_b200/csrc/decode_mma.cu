@@ -24,6 +24,11 @@
 //
 // Every barrier wait is bounded (site 211 in the device error word when a stage never lands);
 // a warp that gives up stops computing and drains its other loads, bounded again, before exit.
+//
+// Fused append (lf_decode_fwd_append): the CTA that holds a session's last page first stores
+// the session's newest token (K and V rows of its KV head) into that page, then loads it.  A
+// newest token without a page of its own past the shared prefix, or with a page id out of
+// range, is not stored and leaves site 212.
 #include "decode_common.cuh"
 #include "sm100_primitives.cuh"
 #include "tmap.cuh"
@@ -96,7 +101,9 @@ split_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
                  const uint16_t* __restrict__ q, const int32_t* __restrict__ bt,
                  const int32_t* __restrict__ seq_lens, float* __restrict__ part_o,
                  float2* __restrict__ part_ml, int Hq, int Hkv, int num_pages, int max_pages,
-                 int pages_per_split, int first_page, int n_slots, float qscale) {
+                 int pages_per_split, int first_page, int n_slots, float qscale,
+                 const uint16_t* __restrict__ k_new, const uint16_t* __restrict__ v_new,
+                 uint16_t* kp_w, uint16_t* vp_w) {
     static_assert(D == 64 || D == 128, "head_dim 64 or 128");
     static_assert(G >= 1 && G <= 8, "a GQA group fills at most the 8 MMA columns");
     using LY = Layout<D, S>;
@@ -111,7 +118,12 @@ split_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
     const int L = min(max(seq_lens[n], 0), max_pages * kPage);
     const int npages = (L + kPage - 1) / kPage;
     const int p_begin = first_page + split * pages_per_split;
-    if (p_begin >= npages) return;
+    if (p_begin >= npages) {
+        // fused append: a session whose newest token would not sit in a page of its own (no
+        // tokens, or none past the shared prefix) has no CTA to store it -- reported, not stored
+        if (k_new != nullptr && split == 0 && threadIdx.x == 0) atomicCAS(&g_device_error, 0, 212);
+        return;
+    }
     const int n_local = min(p_begin + pages_per_split, npages) - p_begin;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -128,6 +140,31 @@ split_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
         sm100::fence_barrier_init();
     }
     __syncwarp();
+
+    // Fused append (k_new / v_new given): the CTA holding the session's last page first stores
+    // the newest token's K and V rows of its KV head at position L - 1, then makes the stores
+    // visible to its own TMA page loads (proxy fence, then a CTA barrier before any warp issues).
+    // No other CTA reads that page: it is the session's own, past the shared-prefix pages, and
+    // other heads' rows of it are other CTAs' rows.
+    if (k_new != nullptr && p_begin + n_local == npages) {
+        constexpr int kChunks = D / 8;                       // 16-byte pieces of a row
+        if (threadIdx.x < 2 * kChunks) {
+            const int pos = L - 1;
+            const int page = bt_row[pos / kPage];
+            if (static_cast<unsigned>(page) < static_cast<unsigned>(num_pages)) {
+                const bool isv = threadIdx.x >= kChunks;
+                const int c = threadIdx.x - (isv ? kChunks : 0);
+                const size_t src = ((size_t)n * Hkv + h) * D;
+                const size_t dst = (((size_t)page * Hkv + h) * kPage + pos % kPage) * D;
+                reinterpret_cast<uint4*>((isv ? vp_w : kp_w) + dst)[c] =
+                    reinterpret_cast<const uint4*>((isv ? v_new : k_new) + src)[c];
+                sm100::fence_proxy_async_global();
+            } else if (threadIdx.x == 0) {
+                atomicCAS(&g_device_error, 0, 212);
+            }
+        }
+        __syncthreads();
+    }
 
     int ids = 0, ids_batch = -1;                   // page ids of 32 pages, one per lane
     // A session's own pages are read once: evicted first from L2, so the split and prefix
@@ -302,7 +339,8 @@ template <int D, int S>
 int launch_d(int G, dim3 grid, cudaStream_t st, const CUtensorMap& mk, const CUtensorMap& mv,
              const uint16_t* q, const int32_t* bt, const int32_t* lens, float* po, float2* pml,
              int Hq, int Hkv, int num_pages, int max_pages, int pps, int first_page, int n_slots,
-             float qscale) {
+             float qscale, const uint16_t* k_new, const uint16_t* v_new, uint16_t* kp_w,
+             uint16_t* vp_w) {
     int rc = LF_OK;
 #define LF_MMA_CASE(GG)                                                                         \
     case GG:                                                                                    \
@@ -310,7 +348,7 @@ int launch_d(int G, dim3 grid, cudaStream_t st, const CUtensorMap& mk, const CUt
         if (rc != LF_OK) return rc;                                                             \
         split_mma_kernel<D, GG, S><<<grid, kThreads, Layout<D, S>::kSmemBytes, st>>>(           \
             mk, mv, q, bt, lens, po, pml, Hq, Hkv, num_pages, max_pages, pps, first_page,       \
-            n_slots, qscale);                                                                   \
+            n_slots, qscale, k_new, v_new, kp_w, vp_w);                                         \
         return LF_OK;
     switch (G) {
         LF_MMA_CASE(1)
@@ -325,11 +363,15 @@ int launch_d(int G, dim3 grid, cudaStream_t st, const CUtensorMap& mk, const CUt
 }  // namespace mma
 
 // Per-session pages of a paged decode: grid (split, KV head, session); partials into the
-// workspace slots [0, max_split) of every (session, query head) row.
+// workspace slots [0, max_split) of every (session, query head) row.  With k_new / v_new
+// ([N][Hkv][D]) each session's newest token is stored into its last page first (fused append).
 int launch_split_mma(dim3 grid, cudaStream_t st, const uint16_t* q, const uint16_t* kp,
                      const uint16_t* vp, const int32_t* bt, const int32_t* lens, float* po,
                      float2* pml, int Hq, int Hkv, int D, int num_pages, int max_pages, int pps,
-                     int first_page, int n_slots, float qscale) {
+                     int first_page, int n_slots, float qscale, const uint16_t* k_new,
+                     const uint16_t* v_new) {
+    uint16_t* kp_w = const_cast<uint16_t*>(kp);
+    uint16_t* vp_w = const_cast<uint16_t*>(vp);
     CUtensorMap mk, mv;
     // pages [P*Hkv][16][D]: box = one page of one head, 64 dims (128-byte swizzled rows).
     const cuuint64_t dims[3] = {(cuuint64_t)D, 16, (cuuint64_t)num_pages * Hkv};
@@ -343,9 +385,10 @@ int launch_split_mma(dim3 grid, cudaStream_t st, const uint16_t* q, const uint16
     if (D == 128)
         return mma::launch_d<128, mma::kStages>(G, grid, st, mk, mv, q, bt, lens, po, pml, Hq, Hkv,
                                                 num_pages, max_pages, pps, first_page, n_slots,
-                                                qscale);
+                                                qscale, k_new, v_new, kp_w, vp_w);
     return mma::launch_d<64, mma::kStages>(G, grid, st, mk, mv, q, bt, lens, po, pml, Hq, Hkv,
-                                           num_pages, max_pages, pps, first_page, n_slots, qscale);
+                                           num_pages, max_pages, pps, first_page, n_slots, qscale,
+                                           k_new, v_new, kp_w, vp_w);
 }
 
 }  // namespace decode

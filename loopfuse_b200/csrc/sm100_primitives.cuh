@@ -153,6 +153,12 @@ __device__ __forceinline__ void st_global_v8(void* p, const uint32_t (&w)[8]) {
                  : "memory");
 }
 
+// Orders this thread's earlier generic-proxy accesses of global memory before later async-proxy
+// (TMA) accesses of it.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // Orders this thread's earlier generic-proxy accesses of shared memory before later
 // async-proxy (bulk copy) accesses.
 __device__ __forceinline__ void fence_proxy_async_smem() {

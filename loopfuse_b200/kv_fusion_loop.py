@@ -214,7 +214,9 @@ class FusionLoop:
                     att.paged_decode(self.qdec[:len(S)], kp, vp, table, lens,
                                      num_prefix_pages=self.n_prefix_pages,
                                      pages_per_split=self._pps, workspace=self._ws)
-            launches += 2 + 4 * c.layers
+            # reserve + gather, then per layer the decode's prefix pass, split and combine (the
+            # graphed iteration fuses the K/V append into the split; eager appends separately)
+            launches += 2 + (3 if self._graph is not None else 4) * c.layers
             own = sum(self._pages(s.current_len) - self.n_prefix_pages for s in S)
             bytes_read += c.layers * (self.n_prefix_pages + own) * self.page_bytes
             bytes_unshared += c.layers * sum(self._pages(s.current_len) for s in S) * self.page_bytes
@@ -232,9 +234,10 @@ class FusionLoop:
 
     def _capture_decode(self, S, dec_idx) -> dict:
         """One decode iteration of every session as a CUDA graph: pool reserve and block-table
-        gather on device buffers, then per layer the K/V append and the paged decode.  Captured
-        in setup, after a read-only decode has initialised the decode kernels; nothing in it
-        allocates."""
+        gather on device buffers, then per layer the paged decode with the new token's K/V append
+        fused in (the split pass stores each session's newest token into its page before reading
+        it; the pages end up as ``write_layer`` would leave them).  Captured in setup, after a
+        read-only decode has initialised the decode kernels; nothing in it allocates."""
         c, pool, n = self.cfg, self.pool, len(S)
         i32 = dict(dtype=torch.int32, device=self.device)
         g = {"start": torch.empty(n, **i32), "ones": torch.ones(n, **i32),
@@ -246,11 +249,12 @@ class FusionLoop:
             pool.reserve_device(dec_idx[0], g["ones"], g["start"], n)
             pool.gather_device(dec_idx[0], n, g["table"], g["lens"])
             for layer in range(c.layers):
-                pool.write_layer(S, g["start"], layer, kb, vb, [1] * n, index=dec_idx)
                 kp, vp = pool.layer_pages(layer)
                 att.paged_decode(qd, kp, vp, g["table"], g["lens"],
                                  num_prefix_pages=self.n_prefix_pages, pages_per_split=self._pps,
-                                 out=g["out"], workspace=self._ws)
+                                 out=g["out"], workspace=self._ws,
+                                 k_new=kb.view(n, c.kv_heads, c.head_dim),
+                                 v_new=vb.view(n, c.kv_heads, c.head_dim))
         g["graph"] = graph
         return g
 

@@ -191,3 +191,59 @@ def test_decode_workspace_16_byte_aligned():
     o2 = att.paged_decode(*args, num_prefix_pages=w.n_prefix_pages, pages_per_split=8, workspace=ws16)
     assert torch.equal(o1, o2)
     _check(o1, _oracle(w)[0], "aligned workspace")
+
+
+@pytest.mark.parametrize("hq,hkv,d,prefix_tokens", [(32, 8, 128, 2048), (32, 8, 128, 0),
+                                                    (16, 4, 64, 1024), (8, 8, 128, 256)])
+def test_decode_fused_append_equals_separate_append(hq, hkv, d, prefix_tokens):
+    """``paged_decode(k_new=, v_new=)`` stores each session's newest token (position L - 1)
+    into its page inside the split pass and attends to it: pages and output are bit-identical
+    to storing the token first and decoding after, and the output matches the oracle."""
+    lengths = [prefix_tokens + x for x in (1, 16, 17, 300, 2049, 33, 1000)]
+    w = decode_inputs(N=len(lengths), Hq=hq, Hkv=hkv, D=d, lengths=lengths,
+                      prefix_tokens=prefix_tokens, seed=14)
+    N = len(lengths)
+    _device_status()                                  # start from a clear error word
+    g = torch.Generator(device="cuda").manual_seed(15)
+    k_new = torch.randn(N, hkv, d, generator=g, device="cuda").bfloat16()
+    v_new = torch.randn(N, hkv, d, generator=g, device="cuda").bfloat16()
+    kp_a, vp_a = w.k_pages.clone(), w.v_pages.clone()
+    for n, L in enumerate(lengths):
+        page = int(w.block_table[n, (L - 1) // 16])
+        kp_a[page, :, (L - 1) % 16] = k_new[n]
+        vp_a[page, :, (L - 1) % 16] = v_new[n]
+    args = dict(num_prefix_pages=w.n_prefix_pages, pages_per_split=8)
+    o_a = att.paged_decode(w.q, kp_a, vp_a, w.block_table, w.seq_lens, **args)
+    kp_b, vp_b = w.k_pages.clone(), w.v_pages.clone()
+    o_b = att.paged_decode(w.q, kp_b, vp_b, w.block_table, w.seq_lens, k_new=k_new, v_new=v_new,
+                           **args)
+    assert torch.equal(kp_a, kp_b) and torch.equal(vp_a, vp_b)
+    assert torch.equal(o_a, o_b)
+    ref = ora.decode_paged(w.q.cpu(), kp_a.cpu(), vp_a.cpu(), w.block_table.cpu(), lengths)[0]
+    _check(o_b, ref, f"fused append hq={hq} hkv={hkv} d={d} prefix={prefix_tokens}")
+    assert _device_status() == 0
+
+
+def test_decode_fused_append_reports_a_token_inside_the_shared_prefix():
+    """A session whose newest token would land inside the shared-prefix pages has no page of its
+    own to store it in: nothing is stored and the device error word reports it (site 212)."""
+    lengths = [1000, 3000]                       # the first ends inside the 2048-token prefix
+    w = decode_inputs(N=2, lengths=lengths, prefix_tokens=2048, seed=16)
+    kp, vp = w.k_pages.clone(), w.v_pages.clone()
+    z = torch.zeros(2, 8, 128, dtype=torch.bfloat16, device="cuda")
+    _device_status()
+    att.paged_decode(w.q, kp, vp, w.block_table, w.seq_lens, num_prefix_pages=w.n_prefix_pages,
+                     pages_per_split=8, k_new=z, v_new=z)
+    torch.cuda.synchronize()
+    assert _device_status() == 212
+    assert torch.equal(kp[w.block_table[0, :w.n_prefix_pages].long()],
+                       w.k_pages[w.block_table[0, :w.n_prefix_pages].long()])
+
+
+def _device_status():
+    import ctypes
+    from loopfuse_b200 import _lib
+    torch.cuda.synchronize()
+    v = ctypes.c_int(0)
+    assert _lib.lib().lf_device_status(ctypes.byref(v)) == _lib.LF_OK
+    return v.value
