@@ -23,4 +23,20 @@ def ring_kv_write(pool, state, new_keys: torch.Tensor, new_values: torch.Tensor,
     return pool.write(state, new_keys, new_values, stream=stream)
 
 
-__all__ = ["ring_kv_decode_kernel", "ring_kv_write"]
+def async_zero_slot(pool, state, stream=None) -> None:
+    """The speculative-prefill hook that zeroed the next ring slot (reference
+    ``kernels/cuda/_cuda_ext.py:93-116``, ``async_zero_next_slot_kernel``).
+
+    A paged session reads only positions below its length, and its pages are reserved when
+    tokens are appended, so there is nothing to clear: this checks its arguments and returns.
+    The dense ring layout ``[slots, L, H, max_seq, D]`` is not supported; passing its tensors
+    raises ``TypeError``."""
+    from ...runtime.kv_pool import KVPool, KVState
+
+    if not isinstance(pool, KVPool) or not isinstance(state, KVState):
+        raise TypeError("async_zero_slot takes (KVPool, KVState): the paged pool replaces the "
+                        "dense ring-buffer cache")
+    pool.prefetch_next_slot(state)
+
+
+__all__ = ["async_zero_slot", "ring_kv_decode_kernel", "ring_kv_write"]

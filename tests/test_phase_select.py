@@ -67,6 +67,42 @@ def test_cuda_names_resolve_to_sm100_ops():
     assert resolve_kernel(mod, fn) is ring_kv_decode_kernel
 
 
+def test_cuda_package_exports_the_reference_names():
+    """The reference's ``kernels/cuda/__init__.py`` exports ``is_available``, ``ring_kv_write``
+    and ``async_zero_slot``; the same names import here.  Without a GPU nothing is available,
+    and the dense ring-slot form of ``async_zero_slot`` is refused, not emulated."""
+    import torch
+
+    from loopfuse_b200.kernels import cuda as kc
+    for name in ("is_available", "ring_kv_write", "async_zero_slot", "agent_prefill_kernel",
+                 "ring_kv_decode_kernel"):
+        assert callable(getattr(kc, name)), name
+    if not torch.cuda.is_available():
+        assert kc.is_available() is False
+    ring = torch.zeros(2, 1, 1, 16, 64, dtype=torch.float16)
+    with pytest.raises(TypeError, match="paged pool"):
+        kc.async_zero_slot(ring, ring, 1)
+
+
+@pytest.mark.gpu
+def test_cuda_package_is_available_on_b200_and_zero_slot_leaves_the_pool_unchanged():
+    import torch
+
+    from loopfuse_b200.kernels import cuda as kc
+    from loopfuse_b200.runtime.kv_pool import KVPool
+    assert kc.is_available()
+    pool = KVPool(num_layers=1, num_heads=2, head_dim=64, max_seq_len=64, max_slots=2,
+                  dtype=torch.bfloat16, device="cuda")
+    st = pool.alloc()
+    k = torch.randn(1, 2, 20, 64, device="cuda").to(torch.bfloat16)
+    kc.ring_kv_write(pool, st, k, -k)
+    before = pool.snapshot()
+    kc.async_zero_slot(pool, st)
+    assert pool.snapshot() == before
+    kr, vr = pool.read(st, 0)
+    assert torch.equal(kr, k[0]) and torch.equal(vr, -k[0])
+
+
 @pytest.mark.parametrize("target", [KernelTarget.TRITON, KernelTarget.PALLAS, KernelTarget.EAGER])
 def test_other_targets_do_not_execute(target):
     for phase in (Phase.PREFILL, Phase.DECODE):
