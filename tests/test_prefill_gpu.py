@@ -46,6 +46,17 @@ def test_prefill_appended_queries(Sq, Sk):
     _run_and_check(1, 4, 1, Sq, Sk, True, seed=Sq + Sk)
 
 
+@pytest.mark.parametrize("B,Hq,Hkv,Sq,Sk,causal", [
+    (2, 8, 2, 300, 300, False),        # head_dim 128 without the causal mask, ragged last tile
+    (1, 16, 2, 256, 640, False),       # more keys than queries, no mask
+    (3, 16, 2, 257, 257, True),        # GQA group 8, a tile with a single row
+    (2, 24, 3, 130, 1000, True),       # group 8 over a long cached context
+    (4, 4, 4, 1, 513, True),           # one new token per (batch, head) over 513 keys
+])
+def test_prefill_more_shapes(B, Hq, Hkv, Sq, Sk, causal):
+    _run_and_check(B, Hq, Hkv, Sq, Sk, causal, seed=B * 1000 + Sq + Sk)
+
+
 @pytest.mark.parametrize("Sq,Sk,causal", [(200, 200, True), (128, 512, True), (77, 300, False)])
 def test_prefill_head_dim_64(Sq, Sk, causal):
     """GPT-2 style 64-dim heads (MHA 12 heads)."""
