@@ -18,6 +18,40 @@ int set_error(int code, const char* fmt, ...) {
 
 void clear_error() { g_err[0] = '\0'; }
 
+// cuCtxGetCurrent / cuCtxGetId, looked up through the runtime so that the library links against
+// the runtime alone.
+typedef int (*CtxGetCurrentFn)(void**);
+typedef int (*CtxGetIdFn)(void*, unsigned long long*);
+
+int current_context_id(unsigned long long* id) {
+    static std::once_flag once;
+    static CtxGetCurrentFn get_current = nullptr;
+    static CtxGetIdFn get_id = nullptr;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<CtxGetCurrentFn>(f);
+        f = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<CtxGetIdFn>(f);
+    });
+    LF_CHECK_ARG(get_current != nullptr && get_id != nullptr,
+                 "context: the driver has no cuCtxGetCurrent / cuCtxGetId");
+    void* ctx = nullptr;
+    LF_CHECK_ARG(get_current(&ctx) == 0, "context: cuCtxGetCurrent failed");
+    if (ctx == nullptr) {                 // nothing current yet: bind the device's primary context
+        int dev = 0;
+        LF_CHECK_CUDA(cudaGetDevice(&dev));
+        LF_CHECK_CUDA(cudaSetDevice(dev));
+        LF_CHECK_ARG(get_current(&ctx) == 0 && ctx != nullptr, "context: no current context");
+    }
+    LF_CHECK_ARG(get_id(ctx, id) == 0, "context: cuCtxGetId failed");
+    return LF_OK;
+}
+
 constexpr int kMaxReaders = 64;
 static DeviceErrorReader g_readers[kMaxReaders];
 static int g_n_readers = 0;

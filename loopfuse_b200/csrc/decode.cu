@@ -278,26 +278,41 @@ extern "C" int lf_decode_set_profile_events(void* ev_begin, void* ev_end) {
 // The shared-prefix partial pass is latency-bound (a few tensor-core work items) while the split
 // kernel is bandwidth-bound, and they write disjoint partial slots: the prefix pass runs on a
 // library-owned stream forked from the caller's (event record / wait, the pattern stream capture
-// supports) and joins back before the combine.  One side stream and its two events per device,
-// created on first use; a mutex keeps concurrent callers' fork/join pairs from interleaving.
+// supports) and joins back before the combine.  One side stream and its two events per CUDA
+// context, created the first time the context decodes (streams and events belong to a context,
+// so they are keyed on its id, not on the device ordinal: after a device reset or with another
+// context current a new set is made); a mutex keeps concurrent callers' fork/join pairs from
+// interleaving.
 namespace {
 struct SideStream {
+    unsigned long long ctx = 0;
     cudaStream_t s = nullptr;
     cudaEvent_t fork = nullptr, join = nullptr;
 };
 std::mutex g_side_mu;
-SideStream g_side[64];
+constexpr int kSideStreams = 64;
+SideStream g_side[kSideStreams];
+int g_side_next = 0;
 
 int side_stream(SideStream** out) {                  // caller holds g_side_mu
-    int dev = 0;
-    LF_CHECK_CUDA(cudaGetDevice(&dev));
-    LF_CHECK_ARG(dev >= 0 && dev < 64, "decode: device index %d out of range", dev);
-    SideStream& ss = g_side[dev];
-    if (ss.s == nullptr) {
-        LF_CHECK_CUDA(cudaStreamCreateWithFlags(&ss.s, cudaStreamNonBlocking));
-        LF_CHECK_CUDA(cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming));
-        LF_CHECK_CUDA(cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming));
-    }
+    unsigned long long id = 0;
+    int rc = current_context_id(&id);
+    if (rc != LF_OK) return rc;
+    for (SideStream& ss : g_side)
+        if (ss.s != nullptr && ss.ctx == id) {
+            *out = &ss;
+            return LF_OK;
+        }
+    // A new context takes the next entry.  Past kSideStreams contexts the oldest entry is
+    // reused; its handles are left alone (they may belong to a context that no longer exists).
+    SideStream& ss = g_side[g_side_next];
+    SideStream fresh;
+    fresh.ctx = id;
+    LF_CHECK_CUDA(cudaStreamCreateWithFlags(&fresh.s, cudaStreamNonBlocking));
+    LF_CHECK_CUDA(cudaEventCreateWithFlags(&fresh.fork, cudaEventDisableTiming));
+    LF_CHECK_CUDA(cudaEventCreateWithFlags(&fresh.join, cudaEventDisableTiming));
+    ss = fresh;
+    g_side_next = (g_side_next + 1) % kSideStreams;
     *out = &ss;
     return LF_OK;
 }
@@ -487,38 +502,6 @@ namespace decode {
 // current, the first time a context calls, and kept for that context.  The cache is keyed on the
 // driver's context id, which is unique for the life of the process: a device reset or a
 // different context current on the same device gets a fresh lookup, never a stale address.
-typedef int (*CtxGetCurrentFn)(void**);
-typedef int (*CtxGetIdFn)(void*, unsigned long long*);
-
-static int current_context_id(unsigned long long* id) {
-    static std::once_flag once;
-    static CtxGetCurrentFn get_current = nullptr;
-    static CtxGetIdFn get_id = nullptr;
-    std::call_once(once, [] {
-        void* f = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            get_current = reinterpret_cast<CtxGetCurrentFn>(f);
-        f = nullptr;
-        if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            get_id = reinterpret_cast<CtxGetIdFn>(f);
-    });
-    LF_CHECK_ARG(get_current != nullptr && get_id != nullptr,
-                 "decode noalloc: the driver has no cuCtxGetCurrent / cuCtxGetId");
-    void* ctx = nullptr;
-    LF_CHECK_ARG(get_current(&ctx) == 0, "decode noalloc: cuCtxGetCurrent failed");
-    if (ctx == nullptr) {                 // nothing current yet: bind the device's primary context
-        int dev = 0;
-        LF_CHECK_CUDA(cudaGetDevice(&dev));
-        LF_CHECK_CUDA(cudaSetDevice(dev));
-        LF_CHECK_ARG(get_current(&ctx) == 0 && ctx != nullptr, "decode noalloc: no current context");
-    }
-    LF_CHECK_ARG(get_id(ctx, id) == 0, "decode noalloc: cuCtxGetId failed");
-    return LF_OK;
-}
-
 static int noalloc_scratch(void** out) {
     static std::mutex mu;
     constexpr int kEntries = 128;
@@ -526,7 +509,7 @@ static int noalloc_scratch(void** out) {
     static void* addr[kEntries] = {nullptr};
     static int next = 0;
     unsigned long long id = 0;
-    int rc = current_context_id(&id);
+    int rc = lf::current_context_id(&id);
     if (rc != LF_OK) return rc;
     std::lock_guard<std::mutex> lock(mu);
     for (int i = 0; i < kEntries; ++i)

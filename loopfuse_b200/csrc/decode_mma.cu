@@ -35,8 +35,6 @@
 
 #include <math.h>
 
-#include <atomic>
-
 namespace lf {
 namespace decode {
 namespace mma {
@@ -320,19 +318,16 @@ split_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
     }
 }
 
+// Dynamic shared-memory opt-in, once per CUDA context.
 template <int D, int G, int S>
 int opt_in() {
-    static std::atomic<uint64_t> done{0};
-    int dev = 0;
-    LF_CHECK_CUDA(cudaGetDevice(&dev));
-    const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
-    if (bit == 0 || (done.load() & bit) == 0) {
+    static PerContextOnce once;
+    return once.run([] {
         LF_CHECK_CUDA(cudaFuncSetAttribute(split_mma_kernel<D, G, S>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            Layout<D, S>::kSmemBytes));
-        done.fetch_or(bit);
-    }
-    return LF_OK;
+        return LF_OK;
+    });
 }
 
 template <int D, int S>

@@ -27,8 +27,6 @@
 #include "sm100_primitives.cuh"
 #include "tmap.cuh"
 
-#include <atomic>
-
 namespace lf {
 namespace gemm {
 
@@ -259,19 +257,16 @@ reduce_kernel(const float* __restrict__ part, uint16_t* __restrict__ y, int M, i
         if (m0 + r < M) y[(size_t)(m0 + r) * N + n] = f32_to_bf16_rn(acc[r]);
 }
 
+// Dynamic shared-memory opt-in, once per CUDA context.
 template <int MT>
 int opt_in() {
-    static std::atomic<uint64_t> done{0};
-    int dev = 0;
-    LF_CHECK_CUDA(cudaGetDevice(&dev));
-    const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
-    if (bit == 0 || (done.load() & bit) == 0) {
+    static PerContextOnce once;
+    return once.run([] {
         LF_CHECK_CUDA(cudaFuncSetAttribute(skinny_kernel<MT>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)Cfg<MT>::kSmemBytes));
-        done.fetch_or(bit);
-    }
-    return LF_OK;
+        return LF_OK;
+    });
 }
 
 inline long long grid_size(long long U, int sm_count) { return U < sm_count ? U : sm_count; }

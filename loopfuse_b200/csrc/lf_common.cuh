@@ -6,6 +6,8 @@
 #include <stdint.h>
 #include <stdio.h>
 
+#include <mutex>
+
 #include "../../include/loopfuse_b200.h"
 
 namespace lf {
@@ -25,6 +27,40 @@ void clear_error();
         if (e_ != cudaSuccess)                                                    \
             return ::lf::set_error(LF_ECUDA, "%s: %s", #expr, cudaGetErrorString(e_)); \
     } while (0)
+
+// Id of the CUDA context current on this thread: the driver's context id, unique for the life of
+// the process.  When no context is current, the device's primary context is made current first.
+int current_context_id(unsigned long long* id);
+
+// A set-up step that belongs to a CUDA context (a kernel's shared-memory opt-in, say), run the
+// first time each context reaches the call site that owns this object.  It is keyed on the
+// context id rather than the device ordinal, so after a device reset, or with another context
+// current on the same device, the step runs again instead of being skipped.  Past kSlots
+// contexts the oldest entry makes room; its step then simply runs again if that context returns.
+class PerContextOnce {
+  public:
+    template <class F>
+    int run(F&& setup) {
+        unsigned long long id = 0;
+        const int rc = current_context_id(&id);
+        if (rc != LF_OK) return rc;
+        std::lock_guard<std::mutex> lock(mu_);
+        for (int i = 0; i < n_; ++i)
+            if (ids_[i] == id) return LF_OK;
+        const int rs = setup();
+        if (rs != LF_OK) return rs;
+        ids_[next_] = id;
+        next_ = (next_ + 1) % kSlots;
+        if (n_ < kSlots) ++n_;
+        return LF_OK;
+    }
+
+  private:
+    static constexpr int kSlots = 64;
+    std::mutex mu_;
+    unsigned long long ids_[kSlots] = {};
+    int n_ = 0, next_ = 0;
+};
 
 // After a <<<>>> launch: report configuration errors without synchronising.
 inline int launch_status(const char* what) {

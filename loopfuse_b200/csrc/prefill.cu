@@ -8,7 +8,6 @@
 // heavy-first queue.
 //
 // This file also launches the core's Prefix instantiation for the decode's shared-prefix pass.
-#include <atomic>
 
 #include "attn_tc2.cuh"
 #include "tmap.cuh"
@@ -17,21 +16,17 @@ using namespace lf;
 
 namespace {
 
-// The dynamic shared-memory opt-in is a per-device setting of the kernel, so it is made once
-// for each device this process launches on (setting it twice is harmless).
+// The dynamic shared-memory opt-in is a setting of the kernel in one CUDA context, so it is made
+// once for each context this process launches in (setting it twice is harmless).
 template <lf::tc2::Mode M, int HD>
 int set_smem_attr() {
-    static std::atomic<uint64_t> done{0};
-    int dev = 0;
-    LF_CHECK_CUDA(cudaGetDevice(&dev));
-    const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
-    if (bit == 0 || (done.load() & bit) == 0) {
+    static lf::PerContextOnce once;
+    return once.run([] {
         LF_CHECK_CUDA(cudaFuncSetAttribute(lf::tc2::attn2_kernel<M, HD>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)lf::tc2::kSmemBytes));
-        done.fetch_or(bit);
-    }
-    return LF_OK;
+        return LF_OK;
+    });
 }
 
 template <int HD>
